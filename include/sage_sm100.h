@@ -1,0 +1,161 @@
+/*
+ * sage_sm100.h — C ABI of libsage_sm100.so, the B200 (sm_100a) implementation of
+ * TriBench's sage_attn path (SageAttention-style INT8-QK attention).
+ *
+ * Everything here is plain C: pointers, sizes and status codes. No C++ exception and
+ * no framework type crosses this boundary. The caller owns every buffer (inputs,
+ * outputs, workspace); the hot path allocates nothing. Every call is asynchronous on the
+ * CUDA stream passed as `stream` (a cudaStream_t, or NULL for the legacy default stream).
+ *
+ * Tensor convention (the reference's "HND" layout, kernels/sage_attn/triton_impl.py:42-48):
+ *   a logical [B, H, S, D] tensor whose last dimension is contiguous, described by three
+ *   element strides {batch, head, seq}. The reference's "NHD" layout ([B, S, H, D],
+ *   triton_impl.py:49-55) is the same logical tensor with strides {S*H*D, D, H*D}.
+ *   Base pointers must be 16-byte aligned and strides multiples of 8 elements (16 bytes);
+ *   head_dim must be 64 or 128.
+ *
+ * Quantised intermediates, all owned by the caller and always contiguous:
+ *   q_i8    int8  [B, Hq,  Sq,  D]      per-128-row-block INT8 Q (sm_scale*log2(e) folded in)
+ *   q_scale fp32  [B, Hq,  ceil(Sq/128)]
+ *   k_i8    int8  [B, Hkv, Skv, D]      per-64-row-block INT8 K (after optional smoothing)
+ *   k_scale fp32  [B, Hkv, ceil(Skv/64)]
+ *   k_mean  fp32  [B, Hkv, D]           per-channel token mean of K (smoothing only)
+ *   v_fp8   e4m3  [B, Hkv, Skv, D]      per-channel scaled V (FP8 P.V mode only)
+ *   v_scale fp32  [B, Hkv, D]
+ */
+#ifndef SAGE_SM100_H_
+#define SAGE_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SAGE_ABI_VERSION 1
+
+/* Status codes. 0 is success; everything else is negative. */
+#define SAGE_OK                    0
+#define SAGE_ERR_INVALID_ARG      -1  /* shape, stride, dtype, alignment or size rejected  */
+#define SAGE_ERR_UNSUPPORTED_ARCH -2  /* device is not sm_100 (B200/GB200)                  */
+#define SAGE_ERR_CUDA             -3  /* a CUDA runtime/driver call failed                  */
+#define SAGE_ERR_TIMEOUT          -4  /* a device-side wait hit its limit (see status API)  */
+#define SAGE_ERR_WORKSPACE        -5  /* workspace pointer NULL or smaller than required    */
+
+/* Element types of q/k/v/o. */
+#define SAGE_DTYPE_F16  0
+#define SAGE_DTYPE_BF16 1
+
+/* P.V modes. */
+#define SAGE_PV_16BIT 0   /* P and V in the input's 16-bit type, fp32 accumulation in TMEM */
+#define SAGE_PV_FP8   1   /* P and V in FP8 e4m3, per-channel V scales, fp32 accumulation  */
+
+/* Quantisation flags. */
+#define SAGE_FLAG_SMOOTH_K 1u  /* subtract K's per-channel token mean before quantising */
+#define SAGE_FLAG_KM_GIVEN 2u  /* with SMOOTH_K: k_mean is an input supplied by the caller
+                                  (the reference's `km` argument) instead of being computed */
+
+/* Device-side status bits reported by sage_device_status(). */
+#define SAGE_DEV_TIMEOUT_PRODUCER 0x1
+#define SAGE_DEV_TIMEOUT_MMA      0x2
+#define SAGE_DEV_TIMEOUT_SOFTMAX  0x4
+#define SAGE_DEV_TIMEOUT_EPILOGUE 0x8
+
+/* ABI version of the loaded library (SAGE_ABI_VERSION at build time). */
+int sage_abi_version(void);
+
+/* Message of the last failing call on this host thread ("" when none). */
+const char* sage_last_error(void);
+
+/*
+ * Bytes of scratch that sage_per_block_int8 / sage_run need for these sizes (the K-mean
+ * and V-absmax partial sums). 0 when neither smoothing nor the FP8 P.V mode is requested.
+ */
+size_t sage_workspace_bytes(int64_t batch, int64_t heads_kv, int64_t seq_kv, int64_t head_dim,
+                            int pv_mode, unsigned flags);
+
+/*
+ * Quantise Q and K (and, with SAGE_FLAG_SMOOTH_K, smooth K first).
+ * Replaces per_block_int8(q, k, km, BLKQ=128, BLKK=64, sm_scale, tensor_layout)
+ *   — kernels/sage_attn/triton_impl.py:35-82, kernel quant_per_block_int8_kernel :7-33.
+ * Q is multiplied by fp32(sm_scale * 1.44269504) (triton_impl.py:69); sm_scale <= 0 means
+ * head_dim**-0.5 (triton_impl.py:60-61). K uses multiplier 1.0 (triton_impl.py:79).
+ * k_mean may be NULL unless SAGE_FLAG_SMOOTH_K is set; it is written (the per-channel mean
+ * is computed here) unless SAGE_FLAG_KM_GIVEN is also set, in which case it is read.
+ * The reference never passes km (triton_impl.py:171-173); given an fp32 km it evaluates
+ * k - km in fp32 exactly as here.
+ */
+int sage_per_block_int8(const void* q, const void* k, int dtype,
+                        int64_t batch, int64_t heads_q, int64_t heads_kv,
+                        int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                        const int64_t q_strides[3], const int64_t k_strides[3],
+                        float sm_scale, unsigned flags,
+                        int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale,
+                        float* k_mean, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Quantise V to FP8 e4m3 with one scale per (batch, head, channel):
+ * v_scale = max_s |v| / 448, v_fp8 = e4m3_rn_satfinite(v / v_scale).
+ * No counterpart in the reference (its P.V runs in fp16, triton_impl.py:111-113); it is
+ * the FP8 P.V extension of the same kernel pack.
+ */
+int sage_quant_v_fp8(const void* v, int dtype, int64_t batch, int64_t heads_kv, int64_t seq_kv,
+                     int64_t head_dim, const int64_t v_strides[3],
+                     uint8_t* v_fp8, float* v_scale, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/*
+ * Fused attention over the quantised operands.
+ * Replaces the _attn_fwd launch (kernels/sage_attn/triton_impl.py:121-160, inner loop
+ * :86-119, grid :186-199): S = dequant(q_i8 . k_i8^T), online softmax in base 2,
+ * O = softmax . V, O stored in the input dtype. Unlike the reference Triton kernel,
+ * `causal` is honoured (key j visible to query i iff j <= i; requires seq_q == seq_kv,
+ * like reference.py:19-22). v is the 16-bit V ({batch, head, seq} strides v_strides)
+ * for SAGE_PV_16BIT, or v_fp8 (contiguous) with v_scale for SAGE_PV_FP8.
+ * GQA: heads_q % heads_kv == 0, query head h reads KV head h / (heads_q / heads_kv).
+ */
+int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+                  const float* k_scale, const void* v, const int64_t v_strides[3],
+                  const float* v_scale, void* o, const int64_t o_strides[3],
+                  int dtype, int pv_mode, int causal,
+                  int64_t batch, int64_t heads_q, int64_t heads_kv,
+                  int64_t seq_q, int64_t seq_kv, int64_t head_dim, void* stream);
+
+/*
+ * Whole path in one call: quantise (+ smooth, + V to FP8) then attend.
+ * Replaces run_sage_attn(q, k, v, causal, sm_scale) — kernels/sage_attn/triton_impl.py:162-200.
+ * The caller provides every intermediate buffer listed at the top of this header
+ * (v_fp8/v_scale only for SAGE_PV_FP8, k_mean only with SAGE_FLAG_SMOOTH_K) and a workspace
+ * of at least sage_workspace_bytes(...) bytes.
+ */
+int sage_run(const void* q, const void* k, const void* v, void* o, int dtype,
+             int64_t batch, int64_t heads_q, int64_t heads_kv,
+             int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+             const int64_t q_strides[3], const int64_t k_strides[3],
+             const int64_t v_strides[3], const int64_t o_strides[3],
+             int causal, float sm_scale, int pv_mode, unsigned flags,
+             int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean,
+             uint8_t* v_fp8, float* v_scale, void* workspace, size_t workspace_bytes,
+             void* stream);
+
+/*
+ * Synchronise `stream`, then read and clear the device-side status word of the current
+ * device (SAGE_DEV_* bits; 0 = no wait ran out). Returns SAGE_OK, or SAGE_ERR_TIMEOUT
+ * when any bit was set, or SAGE_ERR_CUDA.
+ */
+int sage_device_status(int* status_bits, void* stream);
+
+/*
+ * Test hook for the watchdog: launches the attention pipeline's bounded mbarrier wait
+ * on a barrier that nothing completes, with the given limit in microseconds. The wait
+ * gives up, sets SAGE_DEV_TIMEOUT_EPILOGUE and the kernel returns normally, leaving the
+ * context usable. No counterpart in the reference.
+ */
+int sage_watchdog_selftest(unsigned limit_us, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAGE_SM100_H_ */

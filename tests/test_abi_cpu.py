@@ -1,0 +1,117 @@
+"""CPU: the C-ABI library loads, exports every symbol include/sage_sm100.h declares, and rejects
+bad arguments with SAGE_ERR_INVALID_ARG before touching a GPU (no compute call is made here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from tribench_b200 import _native as N
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "sage_sm100.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b(sage_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_expected_entry_points():
+    fns = declared_functions()
+    for name in ("sage_per_block_int8", "sage_attn_fwd", "sage_run", "sage_quant_v_fp8", "sage_workspace_bytes",
+                 "sage_last_error", "sage_abi_version", "sage_device_status"):
+        assert name in fns
+
+
+def test_library_exports_every_declared_symbol():
+    lib = N.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in sage_sm100.h but not exported"
+        assert name in N.SIGNATURES, f"{name} has no ctypes signature in _native.SIGNATURES"
+
+
+def test_abi_version():
+    assert N.load().sage_abi_version() == N.SAGE_ABI_VERSION == 1
+
+
+def test_workspace_bytes():
+    lib = N.load()
+    assert lib.sage_workspace_bytes(2, 32, 8192, 128, N.SAGE_PV_16BIT, 0) == 0
+    ws = lib.sage_workspace_bytes(2, 32, 8192, 128, N.SAGE_PV_16BIT, N.SAGE_FLAG_SMOOTH_K)
+    assert ws == 2 * 32 * (8192 // 512) * 128 * 8
+    ws8 = lib.sage_workspace_bytes(2, 32, 8192, 128, N.SAGE_PV_FP8, N.SAGE_FLAG_SMOOTH_K)
+    assert ws8 == ws + 2 * 32 * 16 * 128 * 4
+
+
+def _dummy(n=1 << 12):
+    buf = (ctypes.c_uint8 * (n + 16))()
+    addr = (ctypes.addressof(buf) + 15) & ~15
+    return buf, ctypes.c_void_p(addr)
+
+
+def _pbi8(head_dim=128, strides=(8 * 128, 8 * 128, 128), flags=0, k_mean=True, ws_bytes=1 << 20):
+    lib = N.load()
+    keep, p = _dummy()
+    s = N.strides3(*strides)
+    return lib.sage_per_block_int8(p, p, N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, head_dim, s, s, ctypes.c_float(0.0),
+                                   flags, p, p, p, p, p if k_mean else None, p, ws_bytes, None)
+
+
+def test_rejects_unsupported_head_dim():
+    assert _pbi8(head_dim=96) == N.SAGE_ERR_INVALID_ARG
+    assert "head_dim" in N.load().sage_last_error().decode()
+
+
+def test_rejects_bad_strides():
+    assert _pbi8(strides=(1024, 1024, 100)) == N.SAGE_ERR_INVALID_ARG
+    assert "stride" in N.load().sage_last_error().decode()
+
+
+def test_smoothing_needs_k_mean_and_workspace():
+    assert _pbi8(flags=N.SAGE_FLAG_SMOOTH_K, k_mean=False) == N.SAGE_ERR_INVALID_ARG
+    assert _pbi8(flags=N.SAGE_FLAG_SMOOTH_K, ws_bytes=0) == N.SAGE_ERR_WORKSPACE
+
+
+def test_attn_rejects_causal_with_unequal_lengths_and_bad_mode():
+    lib = N.load()
+    keep, p = _dummy()
+    s = N.strides3(8 * 128, 8 * 128, 128)
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 1, 1, 1, 1, 8, 16, 128,
+                           None)
+    assert rc == N.SAGE_ERR_INVALID_ARG and "causal" in lib.sage_last_error().decode()
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, 7, 0, 1, 1, 1, 8, 8, 128, None)
+    assert rc == N.SAGE_ERR_INVALID_ARG
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, 5, N.SAGE_PV_16BIT, 0, 1, 1, 1, 8, 8, 128, None)
+    assert rc == N.SAGE_ERR_INVALID_ARG and "dtype" in lib.sage_last_error().decode()
+
+
+def test_rejects_gqa_mismatch_and_empty():
+    lib = N.load()
+    keep, p = _dummy()
+    s = N.strides3(8 * 128, 8 * 128, 128)
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 1, 3, 2, 8, 8, 128,
+                           None)
+    assert rc == N.SAGE_ERR_INVALID_ARG and "multiple" in lib.sage_last_error().decode()
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 1, 1, 1, 0, 8, 128,
+                           None)
+    assert rc == N.SAGE_ERR_INVALID_ARG
+
+
+def test_rejects_misaligned_pointer():
+    lib = N.load()
+    keep, p = _dummy()
+    bad = ctypes.c_void_p(p.value + 4)
+    s = N.strides3(8 * 128, 8 * 128, 128)
+    rc = lib.sage_attn_fwd(bad, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 1, 1, 1, 8, 8, 128,
+                           None)
+    assert rc == N.SAGE_ERR_INVALID_ARG and "aligned" in lib.sage_last_error().decode()
+
+
+def test_error_message_is_cleared_by_next_call():
+    lib = N.load()
+    assert _pbi8(head_dim=96) == N.SAGE_ERR_INVALID_ARG
+    assert lib.sage_last_error().decode() != ""
+    assert lib.sage_workspace_bytes(1, 1, 1, 64, 0, 0) == 0
+    assert _pbi8(strides=(1024, 1024, 100)) == N.SAGE_ERR_INVALID_ARG
+    assert "head_dim" not in lib.sage_last_error().decode()

@@ -1,0 +1,449 @@
+// sage_abi.cu — the C ABI of libsage_sm100.so (declared in include/sage_sm100.h): argument
+// validation, TMA descriptor encoding, kernel launches and error reporting. This is the
+// single translation unit of the library; the kernels live in the included .cuh files.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/sage_sm100.h"
+#include "sage_attn.cuh"
+#include "sage_quant.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define SAGE_CUDA_TRY(expr)                                                               \
+  do {                                                                                    \
+    cudaError_t e_ = (expr);                                                              \
+    if (e_ != cudaSuccess)                                                                \
+      return fail(SAGE_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));         \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mutex;
+int g_arch_ok[kMaxDevices];  // 0 unknown, 1 sm_100, -1 other
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int current_device(int* dev) {
+  SAGE_CUDA_TRY(cudaGetDevice(dev));
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(SAGE_ERR_CUDA, "device ordinal %d out of range", *dev);
+  return SAGE_OK;
+}
+
+int check_arch() {
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  std::lock_guard<std::mutex> lk(g_mutex);
+  if (g_arch_ok[dev] == 0) {
+    int major = 0, minor = 0;
+    SAGE_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    SAGE_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    g_arch_ok[dev] = (major == 10 && minor == 0) ? 1 : -1;
+    if (g_arch_ok[dev] < 0)
+      return fail(SAGE_ERR_UNSUPPORTED_ARCH, "device %d is sm_%d%d; libsage_sm100 needs sm_100", dev, major, minor);
+  }
+  if (g_arch_ok[dev] < 0) return fail(SAGE_ERR_UNSUPPORTED_ARCH, "device %d is not sm_100", dev);
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    SAGE_CUDA_TRY(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn)
+      return fail(SAGE_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  return SAGE_OK;
+}
+
+// Raise the dynamic shared-memory limit of `func` once per (device, kernel).
+template <typename F>
+int ensure_smem(F func, int bytes) {
+  static int done[kMaxDevices];  // one table per kernel instantiation
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  std::lock_guard<std::mutex> lk(g_mutex);
+  if (done[dev] != bytes) {
+    SAGE_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev] = bytes;
+  }
+  return SAGE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_strides(const char* name, const int64_t s[3]) {
+  if (!s) return fail(SAGE_ERR_INVALID_ARG, "%s strides are NULL", name);
+  for (int i = 0; i < 3; ++i)
+    if (s[i] <= 0 || (s[i] % 8) != 0)
+      return fail(SAGE_ERR_INVALID_ARG, "%s stride[%d]=%lld must be a positive multiple of 8 elements", name, i,
+                  (long long)s[i]);
+  return SAGE_OK;
+}
+
+int check_shape(int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D) {
+  if (dtype != SAGE_DTYPE_F16 && dtype != SAGE_DTYPE_BF16)
+    return fail(SAGE_ERR_INVALID_ARG, "dtype %d is neither SAGE_DTYPE_F16 nor SAGE_DTYPE_BF16", dtype);
+  if (D != 64 && D != 128) return fail(SAGE_ERR_INVALID_ARG, "head_dim %lld unsupported (64 or 128)", (long long)D);
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0)
+    return fail(SAGE_ERR_INVALID_ARG, "empty or negative shape B=%lld Hq=%lld Hkv=%lld Sq=%lld Skv=%lld",
+                (long long)B, (long long)Hq, (long long)Hkv, (long long)Sq, (long long)Skv);
+  if (Hq % Hkv != 0)
+    return fail(SAGE_ERR_INVALID_ARG, "heads_q=%lld is not a multiple of heads_kv=%lld", (long long)Hq, (long long)Hkv);
+  if (B > 65535 || Hq > 65535 || Sq > (1LL << 30) || Skv > (1LL << 30))
+    return fail(SAGE_ERR_INVALID_ARG, "shape exceeds launch limits");
+  return SAGE_OK;
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+size_t ws_ksum_bytes(int64_t B, int64_t Hkv, int64_t Skv, int64_t D) {
+  return static_cast<size_t>(B * Hkv * cdiv(Skv, sage::kStatsChunk) * D) * sizeof(double);
+}
+size_t ws_vmax_bytes(int64_t B, int64_t Hkv, int64_t Skv, int64_t D) {
+  return static_cast<size_t>(B * Hkv * cdiv(Skv, sage::kStatsChunk) * D) * sizeof(float);
+}
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int encode_4d(CUtensorMap* map, CUtensorMapDataType dt, int elt_bytes, const void* base, int64_t d0, int64_t d1,
+              int64_t d2, int64_t d3, int64_t s1, int64_t s2, int64_t s3, uint32_t box0, uint32_t box1,
+              CUtensorMapSwizzle sw) {
+  cuuint64_t dims[4] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2, (cuuint64_t)d3};
+  cuuint64_t strides[3] = {(cuuint64_t)(s1 * elt_bytes), (cuuint64_t)(s2 * elt_bytes), (cuuint64_t)(s3 * elt_bytes)};
+  cuuint32_t box[4] = {box0, box1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SAGE_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return SAGE_OK;
+}
+
+// Wall-time limit of every device-side mbarrier wait: 2 s, or SAGE_WAIT_LIMIT_MS if set.
+unsigned long long wait_limit_ns() {
+  static const unsigned long long v = [] {
+    const char* e = std::getenv("SAGE_WAIT_LIMIT_MS");
+    const long long ms = e ? std::atoll(e) : 0;
+    return ms > 0 ? static_cast<unsigned long long>(ms) * 1000000ull : 2000000000ull;
+  }();
+  return v;
+}
+
+// ---------------------------------------------------------------- pre-pass launches
+template <int D, typename T>
+int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                   int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs, float q_mult, bool smooth,
+                   bool km_given, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean,
+                   uint8_t* v_fp8, float* v_scale, void* ws, cudaStream_t st) {
+  const int nchunk = static_cast<int>(cdiv(Skv, sage::kStatsChunk));
+  const bool want_v = v_fp8 != nullptr;
+  const bool want_km = smooth && !km_given;
+  double* ksum = nullptr;
+  float* vmax = nullptr;
+  if (want_km || want_v) {
+    char* w = static_cast<char*>(ws);
+    ksum = want_km ? reinterpret_cast<double*>(w) : nullptr;
+    vmax = want_v ? reinterpret_cast<float*>(w + align256(ws_ksum_bytes(B, Hkv, Skv, D))) : nullptr;
+    sage::StatsParams sp{};
+    sp.k = want_km ? k : nullptr;
+    sp.v = want_v ? v : nullptr;
+    if (want_km) { sp.k_sb = ks[0]; sp.k_sh = ks[1]; sp.k_ss = ks[2]; }
+    if (want_v) { sp.v_sb = vs[0]; sp.v_sh = vs[1]; sp.v_ss = vs[2]; }
+    sp.ksum_part = ksum;
+    sp.vmax_part = vmax;
+    sp.Hkv = (int)Hkv; sp.S = (int)Skv; sp.nchunk = nchunk;
+    sage::kv_stats_kernel<D, T><<<dim3(nchunk, (unsigned)Hkv, (unsigned)B), sage::kQuantThreads, 0, st>>>(sp);
+    SAGE_CUDA_TRY(cudaGetLastError());
+    sage::FinalizeParams fp{};
+    fp.ksum_part = ksum; fp.vmax_part = vmax; fp.k_mean = k_mean; fp.v_scale = v_scale;
+    fp.Hkv = (int)Hkv; fp.S = (int)Skv; fp.nchunk = nchunk; fp.D = D;
+    sage::kv_finalize_kernel<<<dim3((unsigned)Hkv, (unsigned)B), 128, 0, st>>>(fp);
+    SAGE_CUDA_TRY(cudaGetLastError());
+  }
+  sage::QuantParams p{};
+  p.q = q; p.k = k; p.v = want_v ? v : nullptr;
+  if (q) { p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_ss = qs[2]; }
+  if (k) { p.k_sb = ks[0]; p.k_sh = ks[1]; p.k_ss = ks[2]; }
+  if (want_v) { p.v_sb = vs[0]; p.v_sh = vs[1]; p.v_ss = vs[2]; }
+  p.q_i8 = q_i8; p.q_scale = q_scale; p.k_i8 = k_i8; p.k_scale = k_scale;
+  p.k_mean = smooth ? k_mean : nullptr;
+  p.v_fp8 = v_fp8; p.v_scale = v_scale;
+  p.q_mult = q_mult;
+  p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
+  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, 64);
+  p.n_q_ctas = q ? (int)(B * Hq * p.nqb) : 0;
+  p.n_k_ctas = k ? (int)(B * Hkv * p.nkb) : 0;
+  const int64_t n_v = want_v ? B * Hkv * p.nvb : 0;
+  const int64_t total = (int64_t)p.n_q_ctas + p.n_k_ctas + n_v;
+  if (total > 0x7fffffffLL) return fail(SAGE_ERR_INVALID_ARG, "too many quantisation blocks");
+  if (total > 0) {
+    sage::quant_kernel<D, T><<<(unsigned)total, sage::kQuantThreads, 0, st>>>(p);
+    SAGE_CUDA_TRY(cudaGetLastError());
+  }
+  return SAGE_OK;
+}
+
+int prepass_dispatch(int dtype, int64_t D, const void* q, const void* k, const void* v, int64_t B, int64_t Hq,
+                     int64_t Hkv, int64_t Sq, int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                     float q_mult, bool smooth, bool km_given, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale,
+                     float* k_mean, uint8_t* v_fp8, float* v_scale, void* ws, cudaStream_t st) {
+  if (dtype == SAGE_DTYPE_F16) {
+    if (D == 128)
+      return launch_prepass<128, __half>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale, k_i8,
+                                         k_scale, k_mean, v_fp8, v_scale, ws, st);
+    return launch_prepass<64, __half>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale, k_i8,
+                                      k_scale, k_mean, v_fp8, v_scale, ws, st);
+  }
+  if (D == 128)
+    return launch_prepass<128, __nv_bfloat16>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale,
+                                              k_i8, k_scale, k_mean, v_fp8, v_scale, ws, st);
+  return launch_prepass<64, __nv_bfloat16>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale,
+                                           k_i8, k_scale, k_mean, v_fp8, v_scale, ws, st);
+}
+
+// ---------------------------------------------------------------- attention launch
+template <int D, int PV, bool OBF16>
+int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const sage::AttnParams& p,
+                cudaStream_t st) {
+  constexpr int QT = 2;
+  using C = sage::AttnCfg<D, PV, QT>;
+  auto kern = sage::sage_attn_kernel<D, PV, QT, OBF16>;
+  if (int rc = ensure_smem(kern, C::SMEM_BYTES)) return rc;
+  dim3 grid((unsigned)p.n_m_ctas, (unsigned)p.Hq, (unsigned)p.B);
+  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
+  SAGE_CUDA_TRY(cudaGetLastError());
+  return SAGE_OK;
+}
+
+int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale, const void* v,
+              const int64_t* vs, const float* v_scale, void* o, const int64_t* os, int dtype, int pv_mode, int causal,
+              int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, cudaStream_t st) {
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  CUtensorMap tq, tk, tv;
+  const CUtensorMapSwizzle swqk = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (int rc = encode_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q_i8, D, Sq, Hq, B, D, Sq * D, Hq * Sq * D,
+                         (uint32_t)D, 128, swqk))
+    return rc;
+  if (int rc = encode_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k_i8, D, Skv, Hkv, B, D, Skv * D, Hkv * Skv * D,
+                         (uint32_t)D, 128, swqk))
+    return rc;
+  if (fp8) {
+    if (int rc = encode_4d(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, v, D, Skv, Hkv, B, D, Skv * D, Hkv * Skv * D,
+                           (uint32_t)D, 128, swqk))
+      return rc;
+  } else {
+    const CUtensorMapDataType dt =
+        dtype == SAGE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (int rc = encode_4d(&tv, dt, 2, v, D, Skv, Hkv, B, vs[2], vs[1], vs[0], 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  sage::AttnParams p{};
+  p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.o = o;
+  p.o_sb = os[0]; p.o_sh = os[1]; p.o_ss = os[2];
+  p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
+  p.groups = (int)(Hq / Hkv);
+  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64);
+  p.causal = causal ? 1 : 0;
+  p.n_m_ctas = (int)cdiv(Sq, 256);
+  p.wait_limit_ns = wait_limit_ns();
+  const bool obf = dtype == SAGE_DTYPE_BF16;
+  if (D == 128) {
+    if (fp8) return obf ? launch_attn<128, sage::kPvE4M3, true>(tq, tk, tv, p, st)
+                        : launch_attn<128, sage::kPvE4M3, false>(tq, tk, tv, p, st);
+    return obf ? launch_attn<128, sage::kPvBF16, true>(tq, tk, tv, p, st)
+               : launch_attn<128, sage::kPvF16, false>(tq, tk, tv, p, st);
+  }
+  if (fp8) return obf ? launch_attn<64, sage::kPvE4M3, true>(tq, tk, tv, p, st)
+                      : launch_attn<64, sage::kPvE4M3, false>(tq, tk, tv, p, st);
+  return obf ? launch_attn<64, sage::kPvBF16, true>(tq, tk, tv, p, st)
+             : launch_attn<64, sage::kPvF16, false>(tq, tk, tv, p, st);
+}
+
+float q_multiplier(float sm_scale, int64_t D) {
+  const double s = sm_scale > 0.0f ? static_cast<double>(sm_scale) : 1.0 / std::sqrt(static_cast<double>(D));
+  return static_cast<float>(s * 1.44269504);
+}
+
+__global__ void watchdog_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    sage::mbar_init(&bar, 1);
+    abort_flag = 0;
+    sage::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Nothing ever arrives on `bar`: the bounded wait must give up and report.
+    (void)sage::mbar_wait(&bar, 0, &abort_flag, sage::kDevTimeoutEpilogue, limit_ns);
+  }
+  __syncthreads();
+}
+
+}  // namespace
+
+extern "C" {
+
+int sage_abi_version(void) { return SAGE_ABI_VERSION; }
+
+const char* sage_last_error(void) { return g_last_error.c_str(); }
+
+size_t sage_workspace_bytes(int64_t batch, int64_t heads_kv, int64_t seq_kv, int64_t head_dim, int pv_mode,
+                            unsigned flags) {
+  if (batch <= 0 || heads_kv <= 0 || seq_kv <= 0 || head_dim <= 0) return 0;
+  size_t n = 0;
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  if (smooth || fp8) n += align256(ws_ksum_bytes(batch, heads_kv, seq_kv, head_dim));
+  if (fp8) n += align256(ws_vmax_bytes(batch, heads_kv, seq_kv, head_dim));
+  return n;
+}
+
+int sage_per_block_int8(const void* q, const void* k, int dtype, int64_t batch, int64_t heads_q, int64_t heads_kv,
+                        int64_t seq_q, int64_t seq_kv, int64_t head_dim, const int64_t q_strides[3],
+                        const int64_t k_strides[3], float sm_scale, unsigned flags, int8_t* q_i8, float* q_scale,
+                        int8_t* k_i8, float* k_scale, float* k_mean, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  g_last_error.clear();
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  if (int rc = check_strides("q", q_strides)) return rc;
+  if (int rc = check_strides("k", k_strides)) return rc;
+  if (!q || !k || !q_i8 || !q_scale || !k_i8 || !k_scale) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(q_i8) || !aligned16(k_i8))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k/q_i8/k_i8 must be 16-byte aligned");
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
+  const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
+  const size_t need = km_given ? 0 : sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_16BIT, flags);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (int rc = check_arch()) return rc;
+  return prepass_dispatch(dtype, head_dim, q, k, nullptr, batch, heads_q, heads_kv, seq_q, seq_kv, q_strides,
+                          k_strides, nullptr, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8, q_scale, k_i8,
+                          k_scale, k_mean, nullptr, nullptr, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int sage_quant_v_fp8(const void* v, int dtype, int64_t batch, int64_t heads_kv, int64_t seq_kv, int64_t head_dim,
+                     const int64_t v_strides[3], uint8_t* v_fp8, float* v_scale, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_shape(dtype, batch, heads_kv, heads_kv, seq_kv, seq_kv, head_dim)) return rc;
+  if (int rc = check_strides("v", v_strides)) return rc;
+  if (!v || !v_fp8 || !v_scale) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(v) || !aligned16(v_fp8)) return fail(SAGE_ERR_INVALID_ARG, "v/v_fp8 must be 16-byte aligned");
+  const size_t need = sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_FP8, 0);
+  if (!workspace || workspace_bytes < need)
+    return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (int rc = check_arch()) return rc;
+  return prepass_dispatch(dtype, head_dim, nullptr, nullptr, v, batch, heads_kv, heads_kv, seq_kv, seq_kv, nullptr,
+                          nullptr, v_strides, 1.0f, false, false, nullptr, nullptr, nullptr, nullptr, nullptr, v_fp8,
+                          v_scale, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale, const void* v,
+                  const int64_t v_strides[3], const float* v_scale, void* o, const int64_t o_strides[3], int dtype,
+                  int pv_mode, int causal, int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
+                  int64_t seq_kv, int64_t head_dim, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
+    return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
+  if (causal && seq_q != seq_kv)
+    return fail(SAGE_ERR_INVALID_ARG, "causal attention needs seq_q == seq_kv (got %lld, %lld)", (long long)seq_q,
+                (long long)seq_kv);
+  if (int rc = check_strides("o", o_strides)) return rc;
+  if (pv_mode == SAGE_PV_16BIT) {
+    if (int rc = check_strides("v", v_strides)) return rc;
+  } else if (!v_scale) {
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs v_scale");
+  }
+  if (!q_i8 || !q_scale || !k_i8 || !k_scale || !v || !o) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q_i8) || !aligned16(k_i8) || !aligned16(v) || !aligned16(o))
+    return fail(SAGE_ERR_INVALID_ARG, "q_i8/k_i8/v/o must be 16-byte aligned");
+  if (int rc = check_arch()) return rc;
+  return attn_impl(q_i8, q_scale, k_i8, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal, batch,
+                   heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream));
+}
+
+int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch, int64_t heads_q,
+             int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim, const int64_t q_strides[3],
+             const int64_t k_strides[3], const int64_t v_strides[3], const int64_t o_strides[3], int causal,
+             float sm_scale, int pv_mode, unsigned flags, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+             float* k_scale, float* k_mean, uint8_t* v_fp8, float* v_scale, void* workspace,
+             size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
+    return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
+  if (causal && seq_q != seq_kv)
+    return fail(SAGE_ERR_INVALID_ARG, "causal attention needs seq_q == seq_kv (got %lld, %lld)", (long long)seq_q,
+                (long long)seq_kv);
+  if (int rc = check_strides("q", q_strides)) return rc;
+  if (int rc = check_strides("k", k_strides)) return rc;
+  if (int rc = check_strides("v", v_strides)) return rc;
+  if (int rc = check_strides("o", o_strides)) return rc;
+  if (!q || !k || !v || !o || !q_i8 || !q_scale || !k_i8 || !k_scale)
+    return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(q_i8) || !aligned16(k_i8))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o/q_i8/k_i8 must be 16-byte aligned");
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
+  if (fp8 && (!v_fp8 || !v_scale || !aligned16(v_fp8)))
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs 16-byte aligned v_fp8 and v_scale");
+  const size_t need = sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, pv_mode, flags);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (int rc = check_arch()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = prepass_dispatch(dtype, head_dim, q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv, seq_q, seq_kv,
+                                q_strides, k_strides, v_strides, q_multiplier(sm_scale, head_dim), smooth,
+                                smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, q_i8,
+                                q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr,
+                                workspace, st))
+    return rc;
+  return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, v_strides,
+                   fp8 ? v_scale : nullptr, o, o_strides, dtype, pv_mode, causal, batch, heads_q, heads_kv, seq_q,
+                   seq_kv, head_dim, st);
+}
+
+int sage_device_status(int* status_bits, void* stream) {
+  g_last_error.clear();
+  if (!status_bits) return fail(SAGE_ERR_INVALID_ARG, "status_bits is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SAGE_CUDA_TRY(cudaStreamSynchronize(st));
+  int v = 0;
+  SAGE_CUDA_TRY(cudaMemcpyFromSymbol(&v, sage::g_dev_status, sizeof(int)));
+  const int zero = 0;
+  SAGE_CUDA_TRY(cudaMemcpyToSymbol(sage::g_dev_status, &zero, sizeof(int)));
+  *status_bits = v;
+  if (v) return fail(SAGE_ERR_TIMEOUT, "device-side wait timed out (status bits 0x%x)", v);
+  return SAGE_OK;
+}
+
+int sage_watchdog_selftest(unsigned limit_us, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_arch()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  watchdog_selftest_kernel<<<1, 32, 0, st>>>(static_cast<unsigned long long>(limit_us) * 1000ull);
+  SAGE_CUDA_TRY(cudaGetLastError());
+  return SAGE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,281 @@
+"""Host side of the B200 sage_attn path: the reference's operator interface over the C ABI.
+
+Mirrors kernels/sage_attn/triton_impl.py:
+  * ``per_block_int8(q, k, km=None, BLKQ=128, BLKK=64, sm_scale=None, tensor_layout="HND")``
+    — same arguments, same return tuple (q_int8, q_scale, k_int8, k_scale), :35-82;
+  * ``run_sage_attn(q, k, v, causal=False, sm_scale=None)`` — :162-200, exported as ``run``
+    too (the TriBench ``cuda`` variant entry point).
+Differences from the reference are deliberate and documented: ``causal`` is honoured (the
+Triton kernel ignores it), K is smoothed by default (``smooth_k=True``), P.V can run in FP8
+(``pv="fp8"``), and bf16 inputs keep P and V in bf16 instead of casting V to fp16.
+
+torch is used only for device memory, the current stream and dtype/shape bookkeeping; all
+arithmetic runs in libsage_sm100.so. There is no CPU or Triton fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.float16: N.SAGE_DTYPE_F16, torch.bfloat16: N.SAGE_DTYPE_BF16}
+_PV = {"16bit": N.SAGE_PV_16BIT, "fp16": N.SAGE_PV_16BIT, "fp8": N.SAGE_PV_FP8}
+
+
+def _dims(t: torch.Tensor, layout: str):
+    """(B, H, S, D, (batch, head, seq) element strides) of a 4-D tensor in HND or NHD layout."""
+    if t.dim() != 4:
+        raise ValueError(f"expected a 4-D tensor, got shape {tuple(t.shape)}")
+    if t.stride(3) != 1:
+        raise ValueError("the head dimension must be contiguous (stride 1)")
+    if layout == "HND":
+        B, H, S, D = t.shape
+        return B, H, S, D, (t.stride(0), t.stride(1), t.stride(2))
+    if layout == "NHD":
+        B, S, H, D = t.shape
+        return B, H, S, D, (t.stride(0), t.stride(2), t.stride(1))
+    raise ValueError(f"tensor_layout must be 'HND' or 'NHD', got {layout!r}")
+
+
+def _check_tensor(name: str, t: torch.Tensor, dtype=None):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (the sage_attn path has no CPU implementation)")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} has dtype {t.dtype}, expected {dtype}")
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _vp(t: torch.Tensor | None):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def workspace_bytes(batch, heads_kv, seq_kv, head_dim, pv: str = "16bit", smooth_k: bool = True) -> int:
+    flags = N.SAGE_FLAG_SMOOTH_K if smooth_k else 0
+    return int(N.load().sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, _PV[pv], flags))
+
+
+@dataclass
+class SageQuant:
+    """Quantised operands of one call (all contiguous, [B, H, S, D]-ordered)."""
+    q_int8: torch.Tensor
+    q_scale: torch.Tensor
+    k_int8: torch.Tensor
+    k_scale: torch.Tensor
+    k_mean: torch.Tensor | None = None
+    v_fp8: torch.Tensor | None = None
+    v_scale: torch.Tensor | None = None
+
+
+def per_block_int8(q, k, km=None, BLKQ=128, BLKK=64, sm_scale=None, tensor_layout="HND", *, smooth_k=False,
+                   return_km=False):
+    """INT8 per-block quantisation of Q (128-row blocks) and K (64-row blocks).
+
+    Same contract as the reference per_block_int8 (triton_impl.py:35-82): returns
+    (q_int8 [B,Hq,Sq,D], q_scale [B,Hq,ceil(Sq/128)], k_int8 [B,Hkv,Skv,D], k_scale [B,Hkv,ceil(Skv/64)]);
+    ``km`` (broadcastable to [B, Hkv, 1, D]) is subtracted from K in fp32 first. ``smooth_k=True``
+    computes km on the device (the K channel mean); ``return_km`` appends it to the tuple.
+    """
+    if BLKQ != 128 or BLKK != 64:
+        raise ValueError("the sm_100a kernels use BLKQ=128, BLKK=64 (triton_impl.py:166-167)")
+    _check_tensor("q", q)
+    _check_tensor("k", k, q.dtype)
+    if q.dtype not in _DTYPES:
+        raise TypeError(f"q/k must be float16 or bfloat16, got {q.dtype}")
+    if q.device != k.device:
+        raise ValueError("q and k must be on the same device")
+    B, Hq, Sq, D, qs = _dims(q, tensor_layout)
+    Bk, Hkv, Skv, Dk, ks = _dims(k, tensor_layout)
+    if Bk != B or Dk != D:
+        raise ValueError(f"q {tuple(q.shape)} and k {tuple(k.shape)} disagree on batch or head_dim")
+    dev = q.device
+    q_i8 = torch.empty((B, Hq, Sq, D), dtype=torch.int8, device=dev)
+    k_i8 = torch.empty((B, Hkv, Skv, D), dtype=torch.int8, device=dev)
+    q_scale = torch.empty((B, Hq, (Sq + 127) // 128), dtype=torch.float32, device=dev)
+    k_scale = torch.empty((B, Hkv, (Skv + 63) // 64), dtype=torch.float32, device=dev)
+    flags = 0
+    k_mean = None
+    if km is not None:
+        # The reference subtracts km from k by broadcasting (triton_impl.py:39-40): km is
+        # broadcastable to [B, Hkv, 1, D] (HND) or [B, 1, Hkv, D] (NHD).
+        kmt = torch.as_tensor(km, device=dev).to(torch.float32)
+        if tensor_layout == "HND":
+            k_mean = torch.broadcast_to(kmt, (B, Hkv, 1, D))[:, :, 0, :].contiguous()
+        else:
+            k_mean = torch.broadcast_to(kmt, (B, 1, Hkv, D))[:, 0, :, :].contiguous()
+        flags = N.SAGE_FLAG_SMOOTH_K | N.SAGE_FLAG_KM_GIVEN
+    elif smooth_k:
+        k_mean = torch.empty((B, Hkv, D), dtype=torch.float32, device=dev)
+        flags = N.SAGE_FLAG_SMOOTH_K
+    ws_n = 0 if (flags & N.SAGE_FLAG_KM_GIVEN) else workspace_bytes(B, Hkv, Skv, D, "16bit", bool(flags))
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+    lib = N.load()
+    with torch.cuda.device(dev):
+        rc = lib.sage_per_block_int8(
+            _vp(q), _vp(k), _DTYPES[q.dtype], B, Hq, Hkv, Sq, Skv, D, N.strides3(*qs), N.strides3(*ks),
+            ctypes.c_float(0.0 if sm_scale is None else float(sm_scale)), flags,
+            _vp(q_i8), _vp(q_scale), _vp(k_i8), _vp(k_scale), _vp(k_mean), _vp(ws), ws_n, _stream_ptr(dev))
+    N.check("sage_per_block_int8", rc)
+    if return_km:
+        return q_i8, q_scale, k_i8, k_scale, k_mean
+    return q_i8, q_scale, k_i8, k_scale
+
+
+def quant_v_fp8(v, tensor_layout="HND"):
+    """V -> (e4m3 codes as uint8 [B, Hkv, Skv, D], fp32 per-channel scales [B, Hkv, D])."""
+    _check_tensor("v", v)
+    if v.dtype not in _DTYPES:
+        raise TypeError(f"v must be float16 or bfloat16, got {v.dtype}")
+    B, H, S, D, vs = _dims(v, tensor_layout)
+    dev = v.device
+    v8 = torch.empty((B, H, S, D), dtype=torch.uint8, device=dev)
+    vsc = torch.empty((B, H, D), dtype=torch.float32, device=dev)
+    ws_n = workspace_bytes(B, H, S, D, "fp8", False)
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = N.load().sage_quant_v_fp8(_vp(v), _DTYPES[v.dtype], B, H, S, D, N.strides3(*vs), _vp(v8), _vp(vsc),
+                                       _vp(ws), ws_n, _stream_ptr(dev))
+    N.check("sage_quant_v_fp8", rc)
+    return v8, vsc
+
+
+def attn_fwd(quant: SageQuant, v, causal=False, *, pv="16bit", out_dtype=None, tensor_layout="HND", out=None):
+    """Attention over already-quantised operands (the _attn_fwd launch, triton_impl.py:121-160)."""
+    q_i8, k_i8 = quant.q_int8, quant.k_int8
+    B, Hq, Sq, D = q_i8.shape
+    _, Hkv, Skv, _ = k_i8.shape
+    dev = q_i8.device
+    pv_mode = _PV[pv]
+    if pv_mode == N.SAGE_PV_FP8:
+        vv, vs = quant.v_fp8, (Skv * D * Hkv, Skv * D, D)
+        if vv is None or quant.v_scale is None:
+            raise ValueError("pv='fp8' needs quant.v_fp8 and quant.v_scale")
+        if out_dtype is None:
+            raise ValueError("pv='fp8' needs out_dtype")
+        dt = out_dtype
+    else:
+        _check_tensor("v", v)
+        _, _, _, _, vs = _dims(v, tensor_layout)
+        vv, dt = v, v.dtype
+    if out is None:
+        out = torch.empty((B, Hq, Sq, D) if tensor_layout == "HND" else (B, Sq, Hq, D), dtype=dt, device=dev)
+    _, _, _, _, os_ = _dims(out, tensor_layout)
+    with torch.cuda.device(dev):
+        rc = N.load().sage_attn_fwd(
+            _vp(q_i8), _vp(quant.q_scale), _vp(k_i8), _vp(quant.k_scale), _vp(vv), N.strides3(*vs),
+            _vp(quant.v_scale), _vp(out), N.strides3(*os_), _DTYPES[dt], pv_mode, int(bool(causal)),
+            B, Hq, Hkv, Sq, Skv, D, _stream_ptr(dev))
+    N.check("sage_attn_fwd", rc)
+    return out
+
+
+class SagePlan:
+    """Preallocated intermediates for repeated calls on one shape (no per-call allocation).
+
+    ``plan.run(q, k, v, o)`` is one ``sage_run`` C call: pre-pass kernels + attention kernel.
+    """
+
+    def __init__(self, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, dtype, device, *, pv="16bit",
+                 smooth_k=True, causal=False, sm_scale=None):
+        if dtype not in _DTYPES:
+            raise TypeError(f"dtype must be float16 or bfloat16, got {dtype}")
+        self.shape = (batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)
+        self.dtype, self.device = dtype, torch.device(device)
+        self.pv_mode = _PV[pv]
+        self.flags = N.SAGE_FLAG_SMOOTH_K if smooth_k else 0
+        self.causal, self.sm_scale = bool(causal), sm_scale
+        B, Hq, Hkv, Sq, Skv, D = self.shape
+        dev = self.device
+        self.quant = SageQuant(
+            q_int8=torch.empty((B, Hq, Sq, D), dtype=torch.int8, device=dev),
+            q_scale=torch.empty((B, Hq, (Sq + 127) // 128), dtype=torch.float32, device=dev),
+            k_int8=torch.empty((B, Hkv, Skv, D), dtype=torch.int8, device=dev),
+            k_scale=torch.empty((B, Hkv, (Skv + 63) // 64), dtype=torch.float32, device=dev),
+            k_mean=torch.empty((B, Hkv, D), dtype=torch.float32, device=dev) if smooth_k else None,
+            v_fp8=torch.empty((B, Hkv, Skv, D), dtype=torch.uint8, device=dev) if self.pv_mode else None,
+            v_scale=torch.empty((B, Hkv, D), dtype=torch.float32, device=dev) if self.pv_mode else None,
+        )
+        self.ws_bytes = workspace_bytes(B, Hkv, Skv, D, pv, smooth_k)
+        self.ws = torch.empty(max(self.ws_bytes, 1), dtype=torch.uint8, device=dev)
+
+    def run(self, q, k, v, out=None, tensor_layout="HND"):
+        B, Hq, Hkv, Sq, Skv, D = self.shape
+        for name, t, h, s in (("q", q, Hq, Sq), ("k", k, Hkv, Skv), ("v", v, Hkv, Skv)):
+            _check_tensor(name, t, self.dtype)
+            tb, th, ts, td, _ = _dims(t, tensor_layout)
+            if (tb, th, ts, td) != (B, h, s, D):
+                raise ValueError(f"{name} shape {tuple(t.shape)} does not match the plan {self.shape}")
+        if out is None:
+            out = torch.empty((B, Hq, Sq, D) if tensor_layout == "HND" else (B, Sq, Hq, D), dtype=self.dtype,
+                              device=self.device)
+        _check_tensor("out", out, self.dtype)
+        *_, qs = _dims(q, tensor_layout)
+        *_, ks = _dims(k, tensor_layout)
+        *_, vs = _dims(v, tensor_layout)
+        *_, os_ = _dims(out, tensor_layout)
+        qd = self.quant
+        rc = N.load().sage_run(
+            _vp(q), _vp(k), _vp(v), _vp(out), _DTYPES[self.dtype], B, Hq, Hkv, Sq, Skv, D,
+            N.strides3(*qs), N.strides3(*ks), N.strides3(*vs), N.strides3(*os_), int(self.causal),
+            ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)), self.pv_mode, self.flags,
+            _vp(qd.q_int8), _vp(qd.q_scale), _vp(qd.k_int8), _vp(qd.k_scale), _vp(qd.k_mean), _vp(qd.v_fp8),
+            _vp(qd.v_scale), _vp(self.ws), self.ws_bytes, _stream_ptr(self.device))
+        N.check("sage_run", rc)
+        return out
+
+
+def run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=True, tensor_layout="HND",
+                  out=None):
+    """Drop-in for run_sage_attn (triton_impl.py:162-200) on sm_100a.
+
+    q: [B, Hq, Sq, D], k/v: [B, Hkv, Skv, D] (HND; NHD with tensor_layout="NHD"), fp16 or bf16,
+    D in {64, 128}. Returns o with q's shape and dtype.
+    """
+    _check_tensor("q", q)
+    for name, t in (("k", k), ("v", v)):
+        _check_tensor(name, t, q.dtype)
+        if t.device != q.device:
+            raise ValueError(f"{name} is on {t.device}, q on {q.device}")
+    if q.dtype not in _DTYPES:
+        raise TypeError(f"q/k/v must be float16 or bfloat16, got {q.dtype}")
+    B, Hq, Sq, D, _ = _dims(q, tensor_layout)
+    _, Hkv, Skv, _, _ = _dims(k, tensor_layout)
+    plan = SagePlan(B, Hq, Hkv, Sq, Skv, D, q.dtype, q.device, pv=pv, smooth_k=smooth_k, causal=causal,
+                    sm_scale=sm_scale)
+    with torch.cuda.device(q.device):
+        return plan.run(q, k, v, out=out, tensor_layout=tensor_layout)
+
+
+run = run_sage_attn
+
+
+def device_status(device=None) -> int:
+    """Synchronise the current stream and return (and clear) the device watchdog bits; raises
+    SageError(SAGE_ERR_TIMEOUT) when a device-side wait ran out."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    bits = ctypes.c_int(0)
+    with torch.cuda.device(dev):
+        rc = N.load().sage_device_status(ctypes.byref(bits), _stream_ptr(dev))
+    N.check("sage_device_status", rc)
+    return bits.value
+
+
+def watchdog_selftest(limit_us: int = 2000, device=None) -> int:
+    """Run the bounded-wait self test and return the status bits it left (expected: the
+    epilogue-timeout bit). The context stays usable."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    lib = N.load()
+    with torch.cuda.device(dev):
+        N.check("sage_watchdog_selftest", lib.sage_watchdog_selftest(int(limit_us), _stream_ptr(dev)))
+        bits = ctypes.c_int(0)
+        rc = lib.sage_device_status(ctypes.byref(bits), _stream_ptr(dev))
+    if rc not in (N.SAGE_OK, N.SAGE_ERR_TIMEOUT):
+        N.check("sage_device_status", rc)
+    return bits.value
