@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""Benchmark of the sage_attn path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload h8k|c2|c3|c4|c5] [--impl ours|reference]
+
+A step is one pass of the path over one batch: the pre-pass (K smoothing + INT8 Q/K
+quantisation, + FP8 V for c4) followed by the fused attention kernel, on inputs already
+resident in HBM. The default workload is "h8k" — B=2, H=32, S=8192, D=128, fp16, non-causal,
+smoothed K, fp16 P.V — the S=8K D=128 configuration the headline metric is quoted on.
+
+Multi-GPU (torchrun, one process per GPU): weak scaling over the (batch x head) grid. The
+global job at N ranks is the workload with batch N times larger; rank r generates and
+processes its own batches (no collective on the data path). value = total ops of all ranks /
+max-over-ranks device time.
+
+--impl reference times the reference's own algorithm on the host CPU (the reference.py `ref`
+PyTorch path, restated per (batch, head) slice in oracle.ref_attention_torch), one sampled
+head per step, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "sage_attn TOPS (S=8K, D=128) vs INT8 tensor peak"
+UNIT = "TOPS"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", default="h8k", choices=["h8k", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def workload_case(name: str, world: int) -> dict:
+    import tribench_b200 as tb
+
+    case = dict(tb.CONFIGS[name])
+    case["name"] = name
+    case["batch_size_per_rank"] = case["batch_size"]
+    if name == "c5":
+        # the sharded long-context config: the fixed (B x H) grid is split across ranks
+        case["shard"] = "strong"
+    else:
+        case["batch_size"] = case["batch_size"] * world
+        case["shard"] = "weak"
+    return case
+
+
+def read_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"bf16_burst": p.get("bf16_tflops"), "bf16_sustained": p.get("bf16_tflops_sustained"),
+                "hbm": p.get("hbm_gbs"), "source": "measured"}
+    return {"bf16_burst": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
+
+
+def read_traffic() -> dict:
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 100 ms while the warm-up and timed steps run."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        with open(self.file.name) as f:
+            rows = [r.strip().split(", ") for r in f if r.strip()]
+        os.unlink(self.file.name)
+        sm, smax, power, reasons = [], None, [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+                power.append(float(r[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        loaded = [s for s, p in zip(sm, power) if p > 300.0] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+def cpu_baseline(case: dict, seconds: float) -> dict:
+    """The reference's PyTorch `ref` on the host CPU, one (b, h) head at a time (bounded sample)."""
+    import oracle
+    import tribench_b200 as tb
+
+    S, D = case["seq_len"], case["head_dim"]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    one = dict(case, batch_size=1, num_heads=1)
+    inp = tb.make_inputs(one, "cpu", seed=case["seed"], dtype="fp32")
+    ops_head = tb.estimate(dict(one))["ops_alg"]
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oracle.ref_attention_torch(inp["q"], inp["k"], inp["v"], causal=case["causal"])
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(ops_head * n / dt / 1e12, 6), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} head(s) of S={S} D={D} (causal={case['causal']}) through the reference's fp32 "
+                      f"PyTorch ref, {dt:.1f} s, extrapolated per op"}
+
+
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    case = workload_case(args.workload, 1)
+    import oracle
+    import tribench_b200 as tb
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    one = dict(case, batch_size=1, num_heads=1)
+    inp = tb.make_inputs(one, "cpu", seed=case["seed"], dtype="fp32")
+    ops_head = tb.estimate(one)["ops_alg"]
+    for _ in range(args.warmup):
+        oracle.ref_attention_torch(inp["q"], inp["k"], inp["v"], causal=case["causal"])
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.ref_attention_torch(inp["q"], inp["k"], inp["v"], causal=case["causal"])
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = ops_head * len(times) / total / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / len(times), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(case, world),
+        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"one (b,h) head of the workload per step (S={case['seq_len']}, "
+                                   f"D={case['head_dim']}), reference.py ref in fp32 PyTorch on the host"},
+        "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(case: dict, world: int) -> dict:
+    nbytes = 2 * case["batch_size"] * case["num_heads"] * case["seq_len"] * case["head_dim"] // max(1, world)
+    return {
+        "workload": case["name"],
+        "batch": case["batch_size"], "heads": case["num_heads"], "seq_len": case["seq_len"],
+        "head_dim": case["head_dim"], "causal": case["causal"], "input_dtype": case["dtype"],
+        "pv": case["pv"], "smooth_k": True, "sharding": f"(batch x head) grid, {case['shard']} scaling",
+        "parallelism": f"shard{world}",
+        "l2": f"inputs {3 * nbytes / 1e6:.0f} MB per rank > 126 MB L2 (no flush needed)"
+              if 3 * nbytes > L2_BYTES else "L2 flushed between steps",
+    }
+
+
+def run_e2e(args, plan, q, k, v, o, dev, stream, barrier, pg) -> float:
+    """Device time of e2e steps through the public API (SagePlan.run = one sage_run C call) with
+    the step's inputs copied from pinned host memory and its output copied back, max over ranks."""
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        out = plan.run(dq, dk, dv, o)
+        ho.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if pg is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    return e2e_ms
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    rank, world, local = dist_env()
+    import tribench_b200 as tb
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        pg = dist
+    case = workload_case(args.workload, world)
+    B, H, S, D = case["batch_size"], case["num_heads"], case["seq_len"], case["head_dim"]
+    nh_total = B * H
+    lo, hi = rank * nh_total // world, (rank + 1) * nh_total // world
+    inp = tb.make_inputs(case, dev, seed=case["seed"], dtype=case["dtype"], heads=(lo, hi))
+    q, k, v = inp["q"], inp["k"], inp["v"]
+    causal, pv = case["causal"], case["pv"]
+    plan = tb.SagePlan(1, hi - lo, hi - lo, S, S, D, q.dtype, dev, pv=pv, smooth_k=True, causal=causal)
+    o = torch.empty_like(q)
+    est_rank = tb.estimate(dict(case, batch_size=1, num_heads=hi - lo))
+    est_total = tb.estimate(case)
+    stream = torch.cuda.current_stream(dev)
+    flush = None
+    if 3 * q.numel() * q.element_size() <= L2_BYTES:
+        flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    # one step = pre-pass + attention: the two C calls sage_run makes (sage_prepass, then
+    # sage_attn_fwd), split so that CUDA events bracket the attention kernel
+    def step(ev_mid=None, ev_end=None):
+        if flush is not None:
+            flush.zero_()
+        plan.prepass(q, k, v)
+        if ev_mid is not None:
+            ev_mid.record(stream)
+        plan.attention(v, o)
+        if ev_end is not None:
+            ev_end.record(stream)
+
+    # our kernels per step: K-stats + finalize + quantise, then attention
+    launches_per_step = 4
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        time.sleep(0.3)  # let nvidia-smi start before the GPU is loaded
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        assert tb.device_status(dev) == 0
+        # ---- timed region: K steps, device time, max over ranks
+        barrier()
+        torch.cuda.synchronize(dev)
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            step(evs[i][1], evs[i][2])
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    step_ms = [evs[i][0].elapsed_time(evs[i][2]) for i in range(args.steps)]
+    attn_ms = [evs[i][1].elapsed_time(evs[i][2]) for i in range(args.steps)]
+    pre_ms = [evs[i][0].elapsed_time(evs[i][1]) for i in range(args.steps)]
+    status = tb.device_status(dev)
+    if pg is not None:
+        t = torch.tensor([total_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+
+    # ---- end to end through the public API: host (pinned) inputs -> device -> run -> host output
+    e2e_ms = None
+    if args.e2e_steps > 0:
+        e2e_ms = run_e2e(args, plan, q, k, v, o, dev, stream, barrier, pg)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(case, args.cpu_baseline_seconds)
+
+    if rank == 0:
+        ops_total = est_total["ops_alg"]
+        value = ops_total * args.steps / (total_ms * 1e-3) / 1e12
+        peaks = read_peaks()
+        # Attention kernel roofline: QK^T at the INT8 rate (2x the measured dense bf16 rate) and
+        # P.V at the 16-bit rate (fp16 P.V) or the FP8 rate (FP8 P.V); the binding peak for the
+        # mix of equal op counts is the harmonic combination.
+        bf16 = peaks["bf16_sustained"]
+        pv_rate = bf16 if pv != "fp8" else 2 * bf16
+        mixed_peak = (est_rank["ops_qk"] + est_rank["ops_pv"]) / (est_rank["ops_qk"] / (2 * bf16) +
+                                                                  est_rank["ops_pv"] / pv_rate)
+        attn_avg = statistics.mean(attn_ms)
+        achieved = est_rank["ops_alg"] / (attn_avg * 1e-3) / 1e12
+        traffic = read_traffic().get(f"attn_{args.workload}_bytes_per_launch")
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
+            "p50_ms": round(statistics.median(step_ms), 4), "higher_is_better": True,
+            "scaling": "strong" if case["shard"] == "strong" else "weak", "vs_baseline": None,
+            "dtype": "int8 QK^T + " + ("e4m3" if pv == "fp8" else case["dtype"]) + " P.V (fp32 accumulate)",
+            "data": "synthetic (seeded per (batch, head) slab; BASELINE distributions)",
+            "config": config_dict(case, world),
+            "frac_of_int8_peak": round(value / world / (2 * bf16), 4),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(mixed_peak, 1),
+                         "unit": "TFLOP/s", "frac": round(achieved / mixed_peak, 4), "traffic": traffic,
+                         "kernel": "sage_attn_kernel", "peak_source": f"{peaks['source']} bf16 sustained "
+                         f"{bf16} TF/s: QK^T at 2x (INT8), P.V at {'2x (FP8)' if pv == 'fp8' else '1x (fp16)'}",
+                         "attn_ms": round(attn_avg, 4), "prepass_ms": round(statistics.mean(pre_ms), 4)},
+            "prepass_roofline": {"bound": "hbm", "achieved": round(tb.prepass_bytes(dict(case, batch_size=1,
+                                 num_heads=hi - lo)) / (statistics.mean(pre_ms) * 1e-3) / 1e9, 1),
+                                 "peak": peaks["hbm"], "unit": "GB/s",
+                                 "kernels": "kv_stats + kv_finalize + quant (3 launches)"},
+            "clocks": clk.summary(),
+            "e2e": None if e2e_ms is None else {
+                "value": round(ops_total * args.e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT,
+                "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
+                "d2h_bytes_per_step": o.numel() * o.element_size(),
+                "ms_per_step": round(e2e_ms / args.e2e_steps, 3)},
+            "gpu_launches": launches_per_step * args.steps,
+            "device_status": status,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    del plan, q, k, v, o
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

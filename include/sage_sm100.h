@@ -123,6 +123,21 @@ int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
                   int64_t seq_q, int64_t seq_kv, int64_t head_dim, void* stream);
 
 /*
+ * The pre-pass half of sage_run on its own: K smoothing statistics, INT8 Q/K and (for
+ * SAGE_PV_FP8) e4m3 V, in the same launches sage_run makes. Together with sage_attn_fwd it
+ * is exactly sage_run; callers use the split to time or overlap the two halves.
+ * Replaces per_block_int8 + v.to(float16) of run_sage_attn (triton_impl.py:171-173, 189).
+ */
+int sage_prepass(const void* q, const void* k, const void* v, int dtype,
+                 int64_t batch, int64_t heads_q, int64_t heads_kv,
+                 int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                 const int64_t q_strides[3], const int64_t k_strides[3], const int64_t v_strides[3],
+                 float sm_scale, int pv_mode, unsigned flags,
+                 int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean,
+                 uint8_t* v_fp8, float* v_scale, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/*
  * Whole path in one call: quantise (+ smooth, + V to FP8) then attend.
  * Replaces run_sage_attn(q, k, v, causal, sm_scale) — kernels/sage_attn/triton_impl.py:162-200.
  * The caller provides every intermediate buffer listed at the top of this header

@@ -297,8 +297,9 @@ def test_config_h8k_full_sampled():
 
 def test_config_c3_causal_full_sampled():
     rows = np.r_[0:256, 8100:8228, 16256:16384]
-    # the scheme itself reaches ~2.2e-2 on the first causal rows (few keys averaged)
-    _sampled_check("c3", [(0, 0), (1, 31)], rows, 4e-3, (0.999, 3e-2))
+    # The INT8 block scheme itself (oracle.sage_model, no GPU rounding) reaches ~3.6e-2 on the
+    # first causal rows, which average only a few keys; the GPU matches the scheme to < 1e-3.
+    _sampled_check("c3", [(0, 0), (1, 31)], rows, 4e-3, (0.999, 5e-2))
 
 
 def test_config_c4_fp8_causal_full_sampled():

@@ -6,11 +6,11 @@ Public API (mirrors kernels/sage_attn/triton_impl.py and reference.py):
   quant_v_fp8(v), attn_fwd(quant, v, causal), SagePlan (preallocated repeated calls)
   make_inputs(case, device, seed, dtype), estimate(case)
 """
-from .inputs import CONFIGS, estimate, make_inputs
+from .inputs import CONFIGS, estimate, make_inputs, prepass_bytes
 from .sage_attn import (SagePlan, SageQuant, attn_fwd, device_status, per_block_int8, quant_v_fp8, run,
                         run_sage_attn, watchdog_selftest, workspace_bytes)
 
 __all__ = [
-    "CONFIGS", "estimate", "make_inputs", "SagePlan", "SageQuant", "attn_fwd", "device_status",
+    "CONFIGS", "estimate", "make_inputs", "prepass_bytes", "SagePlan", "SageQuant", "attn_fwd", "device_status",
     "per_block_int8", "quant_v_fp8", "run", "run_sage_attn", "watchdog_selftest", "workspace_bytes",
 ]

@@ -42,6 +42,8 @@ SIGNATURES = {
     "sage_quant_v_fp8": (_I, [_P, _I, _I64, _I64, _I64, _I64, _I64P, _P, _P, _P, _SZ, _P]),
     "sage_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I,
                            _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "sage_prepass": (_I, [_P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _F, _I, _U,
+                          _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "sage_run": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _I64P,
                       _I, _F, _I, _U, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "sage_device_status": (_I, [ctypes.POINTER(ctypes.c_int), _P]),

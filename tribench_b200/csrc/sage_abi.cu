@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -74,15 +75,16 @@ int check_arch() {
 }
 
 // Raise the dynamic shared-memory limit of `func` once per (device, kernel).
-template <typename F>
-int ensure_smem(F func, int bytes) {
-  static int done[kMaxDevices];  // one table per kernel instantiation
+std::map<std::pair<const void*, int>, int> g_smem_set;
+
+int ensure_smem(const void* func, int bytes) {
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
   std::lock_guard<std::mutex> lk(g_mutex);
-  if (done[dev] != bytes) {
+  int& cur = g_smem_set[{func, dev}];
+  if (cur != bytes) {
     SAGE_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    done[dev] = bytes;
+    cur = bytes;
   }
   return SAGE_OK;
 }
@@ -224,7 +226,7 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
   constexpr int QT = 2;
   using C = sage::AttnCfg<D, PV, QT>;
   auto kern = sage::sage_attn_kernel<D, PV, QT, OBF16>;
-  if (int rc = ensure_smem(kern, C::SMEM_BYTES)) return rc;
+  if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), C::SMEM_BYTES)) return rc;
   dim3 grid((unsigned)p.n_m_ctas, (unsigned)p.Hq, (unsigned)p.B);
   kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
   SAGE_CUDA_TRY(cudaGetLastError());
@@ -381,6 +383,58 @@ int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, 
                    heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream));
 }
 
+namespace {
+// Shared validation of sage_prepass / sage_run; returns SAGE_OK or the failing status.
+int check_run_args(const void* q, const void* k, const void* v, int dtype, int64_t batch, int64_t heads_q,
+                   int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim, const int64_t* q_strides,
+                   const int64_t* k_strides, const int64_t* v_strides, int pv_mode, unsigned flags,
+                   const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale,
+                   const float* k_mean, const uint8_t* v_fp8, const float* v_scale, const void* workspace,
+                   size_t workspace_bytes) {
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
+    return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
+  if (int rc = check_strides("q", q_strides)) return rc;
+  if (int rc = check_strides("k", k_strides)) return rc;
+  if (int rc = check_strides("v", v_strides)) return rc;
+  if (!q || !k || !v || !q_i8 || !q_scale || !k_i8 || !k_scale)
+    return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(q_i8) || !aligned16(k_i8))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k/v/q_i8/k_i8 must be 16-byte aligned");
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
+  if (fp8 && (!v_fp8 || !v_scale || !aligned16(v_fp8)))
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs 16-byte aligned v_fp8 and v_scale");
+  const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
+  const size_t need =
+      sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, pv_mode, km_given ? 0u : flags);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  return SAGE_OK;
+}
+}  // namespace
+
+int sage_prepass(const void* q, const void* k, const void* v, int dtype, int64_t batch, int64_t heads_q,
+                 int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim, const int64_t q_strides[3],
+                 const int64_t k_strides[3], const int64_t v_strides[3], float sm_scale, int pv_mode,
+                 unsigned flags, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean,
+                 uint8_t* v_fp8, float* v_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_run_args(q, k, v, dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, q_strides,
+                              k_strides, v_strides, pv_mode, flags, q_i8, q_scale, k_i8, k_scale, k_mean, v_fp8,
+                              v_scale, workspace, workspace_bytes))
+    return rc;
+  if (int rc = check_arch()) return rc;
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  return prepass_dispatch(dtype, head_dim, q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv, seq_q, seq_kv,
+                          q_strides, k_strides, v_strides, q_multiplier(sm_scale, head_dim), smooth,
+                          smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, q_i8, q_scale, k_i8, k_scale, k_mean,
+                          fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace,
+                          static_cast<cudaStream_t>(stream));
+}
+
 int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch, int64_t heads_q,
              int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim, const int64_t q_strides[3],
              const int64_t k_strides[3], const int64_t v_strides[3], const int64_t o_strides[3], int causal,
@@ -388,35 +442,23 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
              float* k_scale, float* k_mean, uint8_t* v_fp8, float* v_scale, void* workspace,
              size_t workspace_bytes, void* stream) {
   g_last_error.clear();
-  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
-  if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
-    return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
+  if (int rc = check_run_args(q, k, v, dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, q_strides,
+                              k_strides, v_strides, pv_mode, flags, q_i8, q_scale, k_i8, k_scale, k_mean, v_fp8,
+                              v_scale, workspace, workspace_bytes))
+    return rc;
   if (causal && seq_q != seq_kv)
     return fail(SAGE_ERR_INVALID_ARG, "causal attention needs seq_q == seq_kv (got %lld, %lld)", (long long)seq_q,
                 (long long)seq_kv);
-  if (int rc = check_strides("q", q_strides)) return rc;
-  if (int rc = check_strides("k", k_strides)) return rc;
-  if (int rc = check_strides("v", v_strides)) return rc;
   if (int rc = check_strides("o", o_strides)) return rc;
-  if (!q || !k || !v || !o || !q_i8 || !q_scale || !k_i8 || !k_scale)
-    return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(q_i8) || !aligned16(k_i8))
-    return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o/q_i8/k_i8 must be 16-byte aligned");
-  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
-  const bool fp8 = pv_mode == SAGE_PV_FP8;
-  if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
-  if (fp8 && (!v_fp8 || !v_scale || !aligned16(v_fp8)))
-    return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs 16-byte aligned v_fp8 and v_scale");
-  const size_t need = sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, pv_mode, flags);
-  if (need && (!workspace || workspace_bytes < need))
-    return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (!o || !aligned16(o)) return fail(SAGE_ERR_INVALID_ARG, "o must be a 16-byte aligned pointer");
   if (int rc = check_arch()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
   if (int rc = prepass_dispatch(dtype, head_dim, q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv, seq_q, seq_kv,
                                 q_strides, k_strides, v_strides, q_multiplier(sm_scale, head_dim), smooth,
-                                smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, q_i8,
-                                q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr,
-                                workspace, st))
+                                smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, q_i8, q_scale, k_i8, k_scale, k_mean,
+                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st))
     return rc;
   return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, v_strides,
                    fp8 ? v_scale : nullptr, o, o_strides, dtype, pv_mode, causal, batch, heads_q, heads_kv, seq_q,

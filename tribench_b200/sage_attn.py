@@ -205,6 +205,27 @@ class SagePlan:
         self.ws_bytes = workspace_bytes(B, Hkv, Skv, D, pv, smooth_k)
         self.ws = torch.empty(max(self.ws_bytes, 1), dtype=torch.uint8, device=dev)
 
+    def prepass(self, q, k, v, tensor_layout="HND"):
+        """The pre-pass half of run() (sage_prepass): fills self.quant from q, k (and v for FP8)."""
+        B, Hq, Hkv, Sq, Skv, D = self.shape
+        *_, qs = _dims(q, tensor_layout)
+        *_, ks = _dims(k, tensor_layout)
+        *_, vs = _dims(v, tensor_layout)
+        qd = self.quant
+        rc = N.load().sage_prepass(
+            _vp(q), _vp(k), _vp(v), _DTYPES[self.dtype], B, Hq, Hkv, Sq, Skv, D, N.strides3(*qs), N.strides3(*ks),
+            N.strides3(*vs), ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)), self.pv_mode,
+            self.flags, _vp(qd.q_int8), _vp(qd.q_scale), _vp(qd.k_int8), _vp(qd.k_scale), _vp(qd.k_mean),
+            _vp(qd.v_fp8), _vp(qd.v_scale), _vp(self.ws), self.ws_bytes, _stream_ptr(self.device))
+        N.check("sage_prepass", rc)
+        return self.quant
+
+    def attention(self, v, out, tensor_layout="HND"):
+        """The attention half of run() (sage_attn_fwd) over self.quant."""
+        pv = "fp8" if self.pv_mode == N.SAGE_PV_FP8 else "16bit"
+        return attn_fwd(self.quant, v, self.causal, pv=pv, out_dtype=self.dtype, tensor_layout=tensor_layout,
+                        out=out)
+
     def run(self, q, k, v, out=None, tensor_layout="HND"):
         B, Hq, Hkv, Sq, Skv, D = self.shape
         for name, t, h, s in (("q", q, Hq, Sq), ("k", k, Hkv, Skv), ("v", v, Hkv, Skv)):
