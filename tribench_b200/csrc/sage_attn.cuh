@@ -55,7 +55,7 @@ struct AttnCfg {
   static constexpr int OFF_K = OFF_Q + QT * Q_TILE;
   static constexpr int OFF_V = OFF_K + NS * K_TILE;
   static constexpr int OFF_BAR = OFF_V + NS * V_TILE;
-  static constexpr int NUM_BARS = 1 + 3 * NS + 3 * QT;
+  static constexpr int NUM_BARS = 1 + 3 * NS + 4 * QT;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_USED = OFF_MISC + 16;
   // Pad to > half of the SM's shared memory so that exactly one CTA is resident per SM:
@@ -80,6 +80,13 @@ struct AttnCfg {
       make_idesc(kFmtD_S32, kFmtS8, kFmtS8, 0, 0, BM, BN);
   static constexpr uint32_t PV_FMT = (PV == kPvBF16) ? kFmtBF16 : ((PV == kPvE4M3) ? kFmtE4M3 : kFmtF16);
   static constexpr uint32_t IDESC_PV = make_idesc(kFmtD_F32, PV_FMT, PV_FMT, 0, 1, BM, D);
+  // Softmax: the running max is only raised when a tile's max exceeds it by more than LAZY
+  // (log2 units), so P = 2^(s - m) <= 2^LAZY and O needs rescaling only on those rare tiles.
+  // FP8 P keeps the exact max and is scaled by 2^P_SHIFT into the e4m3 range.
+  static constexpr float LAZY = (PV == kPvE4M3) ? 0.0f : 8.0f;
+  static constexpr float P_SHIFT = (PV == kPvE4M3) ? 8.0f : 0.0f;
+  // Exponentials per 32 columns computed by the FMA-pipe polynomial instead of MUFU.ex2.
+  static constexpr int EMU = 8;
 };
 
 // Bounded-wait limit sentinel codes (match SAGE_DEV_* in sage_sm100.h).
@@ -98,7 +105,8 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
   uint64_t* bar_vfull = bar_kfull + C::NS;
   uint64_t* bar_kvempty = bar_vfull + C::NS;
   uint64_t* bar_sfull = bar_kvempty + C::NS;
-  uint64_t* bar_pfull = bar_sfull + QT;
+  uint64_t* bar_phalf = bar_sfull + QT;
+  uint64_t* bar_pfull = bar_phalf + QT;
   uint64_t* bar_odone = bar_pfull + QT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
@@ -133,6 +141,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
     }
     for (int t = 0; t < QT; ++t) {
       mbar_init(bar_sfull + t, 1);
+      mbar_init(bar_phalf + t, 128);
       mbar_init(bar_pfull + t, 128);
       mbar_init(bar_odone + t, 1);
     }
@@ -202,24 +211,30 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
           if (j >= nkv[t]) continue;
-          if (!mbar_wait(bar_pfull + t, j & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
-          if (!v_ready) {
-            if (!mbar_wait(bar_vfull + s, (j / C::NS) & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
-            v_ready = true;
-          }
-          tc_fence_after();
           const uint64_t vd = make_smem_desc(v_addr + s * C::V_TILE, C::V_LBO, C::V_SBO, C::V_LAYOUT);
           const uint32_t p_tmem = tmem_base + 256 * t + C::P_COL;
           const uint32_t o_tmem = tmem_base + 256 * t + 128;
+          // P.V over the first 64 keys as soon as their P is in TMEM, then the rest
 #pragma unroll
-          for (int kk = 0; kk < C::BN / C::PV_K; ++kk) {
-            const uint64_t vdk = desc_advance(vd, kk * C::PV_K * C::V_ATOM_ROW);
-            if constexpr (PV == kPvE4M3)
-              umma_f8_ts(o_tmem, p_tmem + kk * 8, vdk, C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
-            else
-              umma_f16_ts(o_tmem, p_tmem + kk * 8, vdk, C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int half = 0; half < 2; ++half) {
+            if (!mbar_wait((half ? bar_pfull : bar_phalf) + t, j & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
+            if (!v_ready) {
+              if (!mbar_wait(bar_vfull + s, (j / C::NS) & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
+              v_ready = true;
+            }
+            tc_fence_after();
+            constexpr int NK = C::BN / C::PV_K;  // MMAs per key tile
+#pragma unroll
+            for (int kk = half * NK / 2; kk < (half + 1) * NK / 2; ++kk) {
+              const uint64_t vdk = desc_advance(vd, kk * C::PV_K * C::V_ATOM_ROW);
+              if constexpr (PV == kPvE4M3)
+                umma_f8_ts(o_tmem, p_tmem + kk * 8, vdk, C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+              else
+                umma_f16_ts(o_tmem, p_tmem + kk * 8, vdk, C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
-          umma_commit(bar_odone + t);
+          if (!ok) break;
+          if (j + 1 == nkv[t]) umma_commit(bar_odone + t);  // O_t final once this lands
           if (j + 1 < nkv[t]) {
             const int s1 = (j + 1) % C::NS;
             if (!knext_ready) {
@@ -252,73 +267,90 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
     const float* ksp = p.k_scale + ((size_t)b * p.Hkv + hkv) * p.nkb;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: bit pattern 0x4B400000 + s for |s| < 2^22
     for (int j = 0; j < n; ++j) {
       if (!__all_sync(0xffffffffu, mbar_wait(bar_sfull + t, j & 1, abort_flag, kDevTimeoutSoftmax, p.wait_limit_ns))) { ok = false; break; }
       tc_fence_after();
-      uint32_t sr[128];
-      tmem_ld64_sync(s_tmem, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
-      tmem_ld64_sync(s_tmem + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
-      const int kb0 = 2 * j;
-      const float sc0 = qs * ksp[kb0];
-      const float sc1 = (kb0 + 1 < p.nkb) ? qs * ksp[kb0 + 1] : 0.0f;
-      float sf[128];
+      float b[128];
+      {
+        uint32_t sr[128];
+        tmem_ld128_sync(s_tmem, sr);
+        // int32 score s -> float 12582912 + s exactly (an integer add instead of a conversion);
+        // monotone in s, so maxima can be taken on these biased values.
 #pragma unroll
-      for (int c = 0; c < 128; ++c) sf[c] = i2f_exact22(sr[c]) * (c < 64 ? sc0 : sc1);
+        for (int c = 0; c < 128; ++c) b[c] = __uint_as_float(sr[c] + 0x4B400000u);
+      }
       const int key0 = j * C::BN;
-      const bool need_mask = (key0 + C::BN > p.Skv) || (p.causal && key0 + C::BN - 1 > r0);
-      if (need_mask) {
-        const int lim = p.causal ? min(p.Skv, row + 1) : p.Skv;  // keys [key0, lim) visible
+      if ((key0 + C::BN > p.Skv) || (p.causal && key0 + C::BN - 1 > r0)) {
+        const int lim = (p.causal ? min(p.Skv, row + 1) : p.Skv) - key0;  // visible keys: [0, lim)
 #pragma unroll
         for (int c = 0; c < 128; ++c)
-          if (key0 + c >= lim) sf[c] = -INFINITY;
+          if (c >= lim) b[c] = -INFINITY;
       }
-      float mx = m_run;
+      // maxima of the two 64-key halves (one k_scale each), short dependency chains
+      float hm[2];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, sf[c]);
-      const float m_use = (mx == -INFINITY) ? 0.0f : mx;
-      const float alpha = ex2_approx(m_run - m_use);
-      float rs = 0.0f;
-      uint32_t pk[C::BN * C::V_ELT / 4];
-      if constexpr (PV == kPvE4M3) {
-        // P scaled by 2^8 into e4m3 range (exact power-of-two shift; undone in the epilogue).
-        const float m8 = m_use - 8.0f;
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float a[8];
 #pragma unroll
-        for (int c = 0; c < 128; c += 4) {
-          const float e0 = ex2_approx(sf[c] - m8), e1 = ex2_approx(sf[c + 1] - m8);
-          const float e2 = ex2_approx(sf[c + 2] - m8), e3 = ex2_approx(sf[c + 3] - m8);
-          rs += (e0 + e1) + (e2 + e3);
-          const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(e0, e1), __NV_SATFINITE, __NV_E4M3);
-          const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(e2, e3), __NV_SATFINITE, __NV_E4M3);
-          pk[c / 4] = lo | (hi << 16);
+        for (int i = 0; i < 8; ++i) {
+          const float* v = b + h2 * 64 + i;
+          a[i] = fmaxf(fmax3(fmax3(v[0], v[8], v[16]), v[24], v[32]), fmax3(v[40], v[48], v[56]));
         }
-      } else {
+        hm[h2] = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+      }
+      const int kb0 = 2 * j;
+      // a zero scale (all-zero block) is replaced by FLT_MIN: its scores are exactly 0 either
+      // way, and masked -inf entries stay -inf instead of becoming NaN
+      const float sc0 = fmaxf(qs * ksp[kb0], 1.17549435e-38f);
+      const float sc1 = (kb0 + 1 < p.nkb) ? fmaxf(qs * ksp[kb0 + 1], 1.17549435e-38f) : sc0;
+      const float tmax = fmaxf((hm[0] - kMagic) * sc0, (hm[1] - kMagic) * sc1);
+      const bool upd = tmax > m_run + C::LAZY;
+      const float m_new = upd ? tmax : m_run;
+      const float alpha = upd ? ex2_approx(m_run - m_new) : 1.0f;
+      const bool rescale = j > 0 && __any_sync(0xffffffffu, upd);
+      const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
+      // exponent argument = s*sc - m = b*sc - (12582912*sc + m): one packed FMA per two scores
+      const float cc0 = -fmaf(kMagic, sc0, m_use - C::P_SHIFT);
+      const float cc1 = -fmaf(kMagic, sc1, m_use - C::P_SHIFT);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int c = 0; c < 128; c += 2) {
-          const float e0 = ex2_approx(sf[c] - m_use), e1 = ex2_approx(sf[c + 1] - m_use);
-          rs += e0 + e1;
-          if constexpr (PV == kPvBF16) {
-            __nv_bfloat162 v2 = __floats2bfloat162_rn(e0, e1);
-            pk[c / 2] = *reinterpret_cast<uint32_t*>(&v2);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const float2 scv = h2 ? make_float2(sc1, sc1) : make_float2(sc0, sc0);
+        const float2 ccv = h2 ? make_float2(cc1, cc1) : make_float2(cc0, cc0);
+        constexpr int NW = (PV == kPvE4M3) ? 16 : 32;  // packed P words per 64 keys
+        uint32_t pk[NW];
+#pragma unroll
+        for (int pr = 0; pr < 32; ++pr) {
+          const int c = h2 * 64 + 2 * pr;
+          const float2 a = ffma2(make_float2(b[c], b[c + 1]), scv, ccv);
+          float2 e;
+          if ((c % 32) >= 32 - C::EMU) {
+            e = exp2_poly2(a);
           } else {
-            __half2 v2 = __floats2half2_rn(e0, e1);
-            pk[c / 2] = *reinterpret_cast<uint32_t*>(&v2);
+            e.x = ex2_approx(a.x);
+            e.y = ex2_approx(a.y);
+          }
+          acc[pr & 3] = fadd2(acc[pr & 3], e);
+          if constexpr (PV == kPvE4M3) {
+            const uint32_t w = __nv_cvt_float2_to_fp8x2(e, __NV_SATFINITE, __NV_E4M3);
+            if (pr & 1) pk[pr >> 1] |= w << 16; else pk[pr >> 1] = w;
+          } else if constexpr (PV == kPvBF16) {
+            __nv_bfloat162 v2 = __floats2bfloat162_rn(e.x, e.y);
+            pk[pr] = *reinterpret_cast<uint32_t*>(&v2);
+          } else {
+            __half2 v2 = __floats2half2_rn(e.x, e.y);
+            pk[pr] = *reinterpret_cast<uint32_t*>(&v2);
           }
         }
-      }
-      l_run = l_run * alpha + rs;
-      m_run = mx;
-      // P into TMEM over the upper columns of S_t.
-      if constexpr (PV == kPvE4M3) {
-        tmem_st32(s_tmem + C::P_COL, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      } else {
-        tmem_st32(s_tmem + C::P_COL, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-        tmem_st32(s_tmem + C::P_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-      }
-      if (j > 0) {
-        // O_t *= alpha once PV_t(j-1) has landed.
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_odone + t, (j - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.wait_limit_ns))) { ok = false; break; }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        // P over the upper columns of S_t (the whole S row is already in registers)
+        if constexpr (PV == kPvE4M3)
+          tmem_st16(s_tmem + C::P_COL + 16 * h2, pk);
+        else
+          tmem_st32(s_tmem + C::P_COL + 32 * h2, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+        if (h2 == 0 && rescale) {
+          // O_t *= alpha before any P.V of this tile is released. PV_t(j-1) has completed:
+          // S_t(j) was issued after it and tcgen05 operations complete in order.
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 32) {
             uint32_t orow[32];
@@ -328,14 +360,18 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
             tmem_st32(o_tmem + c0, orow);
           }
         }
+        // hand this half of P (and the rescaled O) to the MMA warp
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive((h2 ? bar_pfull : bar_phalf) + t);
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(bar_pfull + t);
+      const float2 s01 = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+      l_run = fmaf(l_run, alpha, s01.x + s01.y);
+      m_run = m_new;
     }
     // ---------------------------------------------------------- epilogue
     if (ok && n > 0 &&
-        __all_sync(0xffffffffu, mbar_wait(bar_odone + t, (n - 1) & 1, abort_flag, kDevTimeoutEpilogue, p.wait_limit_ns))) {
+        __all_sync(0xffffffffu, mbar_wait(bar_odone + t, 0, abort_flag, kDevTimeoutEpilogue, p.wait_limit_ns))) {
       tc_fence_after();
       const float inv_l = 1.0f / l_run;
       const bool valid = row < p.Sq;

@@ -214,6 +214,27 @@ __device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, uint32_t (&r)[32]
       : "r"(taddr)
       : "memory");
 }
+#define SAGE_R8O(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), \
+                    "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+__device__ __forceinline__ void tmem_ld128_sync(uint32_t taddr, uint32_t (&r)[128]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,"
+      "%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,"
+      "%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,"
+      "%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,"
+      "%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : SAGE_R8O(0), SAGE_R8O(8), SAGE_R8O(16), SAGE_R8O(24), SAGE_R8O(32), SAGE_R8O(40), SAGE_R8O(48),
+        SAGE_R8O(56), SAGE_R8O(64), SAGE_R8O(72), SAGE_R8O(80), SAGE_R8O(88), SAGE_R8O(96), SAGE_R8O(104),
+        SAGE_R8O(112), SAGE_R8O(120)
+      : "r"(taddr)
+      : "memory");
+}
+#undef SAGE_R8O
 __device__ __forceinline__ void tmem_ld64_sync(uint32_t taddr, uint32_t (&r)[64]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
@@ -252,6 +273,54 @@ __device__ __forceinline__ void tmem_st_wait() {
 }
 
 // ------------------------------------------------------------------ math helpers
+// Packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
+        "l"(reinterpret_cast<const uint64_t&>(c)));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return d;
+}
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
+  float2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// Two exp2 on the FMA pipe: Cody-Waite split 2^x = 2^j * 2^f with j = rint(x) (magic-number
+// rounding), f in [-0.5, 0.5], and 2^f from a degree-3 polynomial fitted for this kernel by a
+// Remez exchange on the relative error (max 7.5e-5, below the half-ulp of fp16/bf16/e4m3).
+// x is clamped at -125 so the exponent stays normal; results below 2^-125 are irrelevant once
+// P is rounded to 16 or 8 bits. The exponent j is added straight into the float's bit pattern.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kC0 = 0.9999280571937561f, kC1 = 0.6932609677314758f;
+  constexpr float kC2 = 0.2426111251115799f, kC3 = 0.0551716685295105f;
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = fadd2(x, make_float2(12582912.0f, 12582912.0f));   // 1.5*2^23 + rint(x)
+  const float2 j = fadd2(t, make_float2(-12582912.0f, -12582912.0f));  // rint(x)
+  const float2 f = fsub2(x, j);
+  float2 p = ffma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  p = ffma2(p, f, make_float2(kC1, kC1));
+  p = ffma2(p, f, make_float2(kC0, kC0));
+  // the low bits of t hold j; shifting them into the exponent field adds j to it
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
