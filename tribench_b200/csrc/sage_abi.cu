@@ -488,4 +488,13 @@ int sage_watchdog_selftest(unsigned limit_us, void* stream) {
   return SAGE_OK;
 }
 
+#ifdef SAGE_TIMING
+// Profiling build only: copy the per-warp phase timers of the last attention launches.
+int sage_debug_phase_cycles(unsigned long long* host, size_t count) {
+  const size_t n = count < sizeof(sage::g_phase_cycles) / 8 ? count : sizeof(sage::g_phase_cycles) / 8;
+  SAGE_CUDA_TRY(cudaMemcpyFromSymbol(host, sage::g_phase_cycles, n * 8));
+  return SAGE_OK;
+}
+#endif
+
 }  // extern "C"

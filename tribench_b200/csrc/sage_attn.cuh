@@ -55,14 +55,20 @@ struct AttnCfg {
   static constexpr int OFF_K = OFF_Q + QT * Q_TILE;
   static constexpr int OFF_V = OFF_K + NS * K_TILE;
   static constexpr int OFF_BAR = OFF_V + NS * V_TILE;
-  static constexpr int NUM_BARS = 1 + 3 * NS + 4 * QT;
+  static constexpr int NUM_BARS = 1 + 3 * NS + 5 * QT;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_USED = OFF_MISC + 16;
   // Pad to > half of the SM's shared memory so that exactly one CTA is resident per SM:
   // each CTA allocates all 512 TMEM columns when QT == 2.
   static constexpr int SMEM_MIN = (QT == 2) ? 118 * 1024 : 0;
   static constexpr int SMEM_BYTES = 1024 + (SMEM_USED > SMEM_MIN ? SMEM_USED : SMEM_MIN);
-  static constexpr int NUM_THREADS = 32 * (4 * QT + 2);
+  // softmax warpgroups, then one warpgroup with the producer, the MMA issuer and two idle warps
+  static constexpr int NUM_THREADS = 32 * (4 * QT + 4);
+  // Launch allocation 168 registers/thread (3 warps per SM sub-partition); the softmax
+  // warpgroups take 216, the producer/MMA warpgroup keeps 72:
+  // 4*QT*32*216 + 128*72 <= NUM_THREADS*168 for QT = 2 (55296 + 9216 = 64512).
+  static constexpr int REGS_SOFTMAX = 216;
+  static constexpr int REGS_OTHER = 72;
   static constexpr int TMEM_COLS = (QT == 2) ? 512 : 256;
   // K-major operands: SW128 for 128-byte rows, SW64 for 64-byte rows.
   static constexpr uint32_t QK_LAYOUT = (D == 128) ? kLayoutSW128 : kLayoutSW64;
@@ -86,7 +92,11 @@ struct AttnCfg {
   static constexpr float LAZY = (PV == kPvE4M3) ? 0.0f : 8.0f;
   static constexpr float P_SHIFT = (PV == kPvE4M3) ? 8.0f : 0.0f;
   // Exponentials per 32 columns computed by the FMA-pipe polynomial instead of MUFU.ex2.
-  static constexpr int EMU = 8;
+#ifdef SAGE_EMU_PER_32
+  static constexpr int EMU = SAGE_EMU_PER_32;
+#else
+  static constexpr int EMU = 12;
+#endif
 };
 
 // Bounded-wait limit sentinel codes (match SAGE_DEV_* in sage_sm100.h).
@@ -108,6 +118,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
   uint64_t* bar_phalf = bar_sfull + QT;
   uint64_t* bar_pfull = bar_phalf + QT;
   uint64_t* bar_odone = bar_pfull + QT;
+  uint64_t* bar_turn = bar_odone + QT;  // [tile]: the other tile finished its exponentials
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -144,6 +155,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
       mbar_init(bar_phalf + t, 128);
       mbar_init(bar_pfull + t, 128);
       mbar_init(bar_odone + t, 1);
+      mbar_init(bar_turn + t, 4);  // one arrival per warp of the other tile
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -162,8 +174,14 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  if (warp >= 4 * QT) {
+  // ---------------------------------------------------------------- producer / MMA warpgroup
+#ifndef SAGE_NO_SETMAXNREG
+  regs_dec<C::REGS_OTHER>();
+#endif
   if (warp == 4 * QT) {
     // ------------------------------------------------------------ TMA producer
+    SAGE_T_DECL
     if (elect_one() && nkv_max > 0) {
       mbar_arrive_expect_tx(bar_q, QT * C::Q_TILE);
 #pragma unroll
@@ -171,9 +189,11 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
         tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE, &tmQ, bar_q, 0, (m_cta * QT + t) * C::BM, h, b);
       for (int j = 0; j < nkv_max; ++j) {
         const int s = j % C::NS;
+        SAGE_T_MARK(1)
         if (j >= C::NS) {
           if (!mbar_wait(bar_kvempty + s, ((j / C::NS) - 1) & 1, abort_flag, kDevTimeoutProducer, p.wait_limit_ns)) break;
         }
+        SAGE_T_MARK(0)
         mbar_arrive_expect_tx(bar_kfull + s, C::K_TILE);
         tma_load_4d(smem + C::OFF_K + s * C::K_TILE, &tmK, bar_kfull + s, 0, j * C::BN, hkv, b);
         mbar_arrive_expect_tx(bar_vfull + s, C::V_TILE);
@@ -183,8 +203,10 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
                       x * (128 / C::V_ELT), j * C::BN, hkv, b);
       }
     }
+    SAGE_T_FLUSH(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), warp)
   } else if (warp == 4 * QT + 1) {
     // ------------------------------------------------------------ MMA issuer
+    SAGE_T_DECL
     if (elect_one() && nkv_max > 0) {
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
       const uint32_t k_addr = smem_u32(smem + C::OFF_K);
@@ -217,10 +239,13 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
           // P.V over the first 64 keys as soon as their P is in TMEM, then the rest
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
+            SAGE_T_MARK(4)
             if (!mbar_wait((half ? bar_pfull : bar_phalf) + t, j & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
+            SAGE_T_MARK(half)
             if (!v_ready) {
               if (!mbar_wait(bar_vfull + s, (j / C::NS) & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
               v_ready = true;
+              SAGE_T_MARK(2)
             }
             tc_fence_after();
             constexpr int NK = C::BN / C::PV_K;  // MMAs per key tile
@@ -238,7 +263,9 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
           if (j + 1 < nkv[t]) {
             const int s1 = (j + 1) % C::NS;
             if (!knext_ready) {
+              SAGE_T_MARK(4)
               if (!mbar_wait(bar_kfull + s1, ((j + 1) / C::NS) & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
+              SAGE_T_MARK(3)
               knext_ready = true;
               tc_fence_after();
             }
@@ -253,8 +280,23 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
         umma_commit(bar_kvempty + s);  // K_s / V_s reusable once every MMA issued so far is done
       }
     }
+    SAGE_T_FLUSH(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), warp)
+  }
+  // Leave from this branch (warps of the two kinds run with different register budgets):
+  // the MMA warp, which owns TMEM, frees it once every warp has arrived on named barrier 2.
+  tc_fence_before();
+  if (warp == 4 * QT + 1) {
+    asm volatile("bar.sync 2, %0;" ::"n"(C::NUM_THREADS) : "memory");
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  } else {
+    asm volatile("bar.arrive 2, %0;" ::"n"(C::NUM_THREADS) : "memory");
+  }
   } else {
     // ------------------------------------------------------------ softmax warpgroups
+#ifndef SAGE_NO_SETMAXNREG
+    regs_inc<C::REGS_SOFTMAX>();
+#endif
     const int t = warp / 4;
     const int row_in_tile = (warp % 4) * 32 + lane;
     const int r0 = (m_cta * QT + t) * C::BM;
@@ -267,10 +309,13 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
     const float* ksp = p.k_scale + ((size_t)b * p.Hkv + hkv) * p.nkb;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
+    SAGE_T_DECL
     constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: bit pattern 0x4B400000 + s for |s| < 2^22
     for (int j = 0; j < n; ++j) {
+      SAGE_T_MARK(5)
       if (!__all_sync(0xffffffffu, mbar_wait(bar_sfull + t, j & 1, abort_flag, kDevTimeoutSoftmax, p.wait_limit_ns))) { ok = false; break; }
       tc_fence_after();
+      SAGE_T_MARK(0)
       float b[128];
       {
         uint32_t sr[128];
@@ -280,6 +325,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) b[c] = __uint_as_float(sr[c] + 0x4B400000u);
       }
+      SAGE_T_MARK(1)
       const int key0 = j * C::BN;
       if ((key0 + C::BN > p.Skv) || (p.causal && key0 + C::BN - 1 > r0)) {
         const int lim = (p.causal ? min(p.Skv, row + 1) : p.Skv) - key0;  // visible keys: [0, lim)
@@ -309,11 +355,23 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
       const float m_new = upd ? tmax : m_run;
       const float alpha = upd ? ex2_approx(m_run - m_new) : 1.0f;
       const bool rescale = j > 0 && __any_sync(0xffffffffu, upd);
+      SAGE_T_MARK(2)
       const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
       // exponent argument = s*sc - m = b*sc - (12582912*sc + m): one packed FMA per two scores
       const float cc0 = -fmaf(kMagic, sc0, m_use - C::P_SHIFT);
       const float cc1 = -fmaf(kMagic, sc1, m_use - C::P_SHIFT);
       float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#ifdef SAGE_PINGPONG
+      // Ping-pong: the two query tiles take turns on the exponentials (tile 0 of key tile j,
+      // tile 1 of key tile j, tile 0 of key tile j+1, ...), so one tile's MUFU/FMA work overlaps
+      // the other tile's loads, maxima and MMAs instead of competing with its exponentials.
+      if constexpr (QT == 2) {
+        const int n_other = nkv[t ^ 1];
+        const bool must_wait = (t == 1) ? (j < min(n, n_other)) : (j >= 1 && j < min(n, n_other + 1));
+        if (must_wait &&
+            !__all_sync(0xffffffffu, mbar_wait(bar_turn + t, (t == 1 ? j : j - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.wait_limit_ns))) { ok = false; break; }
+      }
+#endif
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         const float2 scv = h2 ? make_float2(sc1, sc1) : make_float2(sc0, sc0);
@@ -343,6 +401,13 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
             pk[pr] = *reinterpret_cast<uint32_t*>(&v2);
           }
         }
+        if (h2 == 1) {
+          // Release the first half of P (stored before these exponentials were computed, so
+          // its TMEM store has completed in their shadow) and the rescaled O.
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(bar_phalf + t);
+        }
         // P over the upper columns of S_t (the whole S row is already in registers)
         if constexpr (PV == kPvE4M3)
           tmem_st16(s_tmem + C::P_COL + 16 * h2, pk);
@@ -360,15 +425,23 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
             tmem_st32(o_tmem + c0, orow);
           }
         }
-        // hand this half of P (and the rescaled O) to the MMA warp
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive((h2 ? bar_pfull : bar_phalf) + t);
+        SAGE_T_MARK(3 + h2)
       }
+#ifdef SAGE_PINGPONG
+      if constexpr (QT == 2) {
+        const int n_other = nkv[t ^ 1];
+        const bool give = (t == 0) ? (j < min(n, n_other)) : (j < min(n_other - 1, n));
+        if (give && lane == 0) mbar_arrive(bar_turn + (t ^ 1));
+      }
+#endif
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar_pfull + t);
       const float2 s01 = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
       l_run = fmaf(l_run, alpha, s01.x + s01.y);
       m_run = m_new;
     }
+    SAGE_T_MARK(5)
     // ---------------------------------------------------------- epilogue
     if (ok && n > 0 &&
         __all_sync(0xffffffffu, mbar_wait(bar_odone + t, 0, abort_flag, kDevTimeoutEpilogue, p.wait_limit_ns))) {
@@ -407,14 +480,10 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
         }
       }
     }
-  }
-
-  // ------------------------------------------------------------ teardown
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 4 * QT + 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    SAGE_T_MARK(6)
+    SAGE_T_FLUSH(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), warp)
+    tc_fence_before();
+    asm volatile("bar.arrive 2, %0;" ::"n"(C::NUM_THREADS) : "memory");
   }
 }
 

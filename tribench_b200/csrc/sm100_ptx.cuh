@@ -43,6 +43,30 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// ------------------------------------------------------------------ phase timers
+// Built only with -DSAGE_TIMING (a profiling build): each warp accumulates clock64() deltas of
+// its pipeline phases and lane 0 writes them to g_phase_cycles[cta % 1024][warp][phase].
+#ifdef SAGE_TIMING
+__device__ unsigned long long g_phase_cycles[1024][20][8];
+#define SAGE_T_DECL                      \
+  unsigned long long _t_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}; \
+  long long _t_last = clock64();
+#define SAGE_T_MARK(k)                   \
+  {                                      \
+    const long long _n = clock64();      \
+    _t_acc[k] += _n - _t_last;           \
+    _t_last = _n;                        \
+  }
+#define SAGE_T_FLUSH(cta, w)                                                   \
+  if ((threadIdx.x & 31) == 0) {                                              \
+    for (int _k = 0; _k < 8; ++_k) g_phase_cycles[(cta) % 1024][w][_k] = _t_acc[_k]; \
+  }
+#else
+#define SAGE_T_DECL
+#define SAGE_T_MARK(k)
+#define SAGE_T_FLUSH(cta, w)
+#endif
+
 // ------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
@@ -270,6 +294,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 #undef SAGE_W8
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Register reallocation between warpgroups (all four warps of a warpgroup execute it). The
+// increments are satisfied from registers released by decrements within the CTA, so the
+// caller must keep sum(threads x registers) within the launch allocation.
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ------------------------------------------------------------------ math helpers
