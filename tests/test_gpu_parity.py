@@ -306,3 +306,23 @@ def test_config_c4_fp8_causal_full_sampled():
     rows = np.r_[0:128, 4000:4128, 8064:8192]
     # FP8 P.V: error measured relative to each channel's |V| max; e4m3 V/P limit max-abs
     _sampled_check("c4", [(0, 0), (7, 15)], rows, 2.5e-2, (0.998, 0.5))
+
+
+def test_quant_full_size_c2_heads_bit_exact():
+    """Full C2 tensors through the pre-pass (smoothing on); sampled heads bit-exact vs the oracle."""
+    case = dict(tb.CONFIGS["c2"])
+    inp = tb.make_inputs(case, DEV, seed=case["seed"], dtype="fp16")
+    q, k = inp["q"], inp["k"]
+    qi, qs, ki, ks, km = tb.per_block_int8(q, k, smooth_k=True, return_km=True)
+    no_timeout()
+    for b, h in [(0, 0), (1, 7), (3, 31)]:
+        qf = f32(q[b:b + 1, h:h + 1])
+        kf = f32(k[b:b + 1, h:h + 1])
+        km_o = oracle.k_mean(kf)
+        np.testing.assert_array_equal(km[b:b + 1, h:h + 1].cpu().numpy(), km_o)
+        qi_o, qs_o = oracle.quant_per_block_int8(qf, 128, oracle.q_multiplier(None, 128))
+        ki_o, ks_o = oracle.quant_per_block_int8(kf, 64, 1.0, km=km_o)
+        np.testing.assert_array_equal(qi[b:b + 1, h:h + 1].cpu().numpy(), qi_o)
+        np.testing.assert_array_equal(qs[b:b + 1, h:h + 1].cpu().numpy(), qs_o)
+        np.testing.assert_array_equal(ki[b:b + 1, h:h + 1].cpu().numpy(), ki_o)
+        np.testing.assert_array_equal(ks[b:b + 1, h:h + 1].cpu().numpy(), ks_o)

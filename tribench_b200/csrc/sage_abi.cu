@@ -155,30 +155,8 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
                    uint8_t* v_fp8, float* v_scale, void* ws, cudaStream_t st) {
   const int nchunk = static_cast<int>(cdiv(Skv, sage::kStatsChunk));
   const bool want_v = v_fp8 != nullptr;
-  const bool want_km = smooth && !km_given;
-  double* ksum = nullptr;
-  float* vmax = nullptr;
-  if (want_km || want_v) {
-    char* w = static_cast<char*>(ws);
-    ksum = want_km ? reinterpret_cast<double*>(w) : nullptr;
-    vmax = want_v ? reinterpret_cast<float*>(w + align256(ws_ksum_bytes(B, Hkv, Skv, D))) : nullptr;
-    sage::StatsParams sp{};
-    sp.k = want_km ? k : nullptr;
-    sp.v = want_v ? v : nullptr;
-    if (want_km) { sp.k_sb = ks[0]; sp.k_sh = ks[1]; sp.k_ss = ks[2]; }
-    if (want_v) { sp.v_sb = vs[0]; sp.v_sh = vs[1]; sp.v_ss = vs[2]; }
-    sp.ksum_part = ksum;
-    sp.vmax_part = vmax;
-    sp.Hkv = (int)Hkv; sp.S = (int)Skv; sp.nchunk = nchunk;
-    sage::kv_stats_kernel<D, T><<<dim3(nchunk, (unsigned)Hkv, (unsigned)B), sage::kQuantThreads, 0, st>>>(sp);
-    SAGE_CUDA_TRY(cudaGetLastError());
-    sage::FinalizeParams fp{};
-    fp.ksum_part = ksum; fp.vmax_part = vmax; fp.k_mean = k_mean; fp.v_scale = v_scale;
-    fp.Hkv = (int)Hkv; fp.S = (int)Skv; fp.nchunk = nchunk; fp.D = D;
-    sage::kv_finalize_kernel<<<dim3((unsigned)Hkv, (unsigned)B), 128, 0, st>>>(fp);
-    SAGE_CUDA_TRY(cudaGetLastError());
-  }
-  sage::QuantParams p{};
+  const bool want_km = smooth && !km_given && k != nullptr;
+  sage::PrepassParams p{};
   p.q = q; p.k = k; p.v = want_v ? v : nullptr;
   if (q) { p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_ss = qs[2]; }
   if (k) { p.k_sb = ks[0]; p.k_sh = ks[1]; p.k_ss = ks[2]; }
@@ -188,15 +166,46 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
   p.v_fp8 = v_fp8; p.v_scale = v_scale;
   p.q_mult = q_mult;
   p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
-  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, 64);
-  p.n_q_ctas = q ? (int)(B * Hq * p.nqb) : 0;
-  p.n_k_ctas = k ? (int)(B * Hkv * p.nkb) : 0;
+  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, 64); p.nchunk = nchunk;
+  const int64_t n_q = q ? B * Hq * p.nqb : 0;
+  const int64_t n_k = k ? B * Hkv * p.nkb : 0;
   const int64_t n_v = want_v ? B * Hkv * p.nvb : 0;
-  const int64_t total = (int64_t)p.n_q_ctas + p.n_k_ctas + n_v;
-  if (total > 0x7fffffffLL) return fail(SAGE_ERR_INVALID_ARG, "too many quantisation blocks");
-  if (total > 0) {
-    sage::quant_kernel<D, T><<<(unsigned)total, sage::kQuantThreads, 0, st>>>(p);
+  const bool need_stats = want_km || want_v;
+  const int64_t n_stat = need_stats ? B * Hkv * nchunk : 0;
+  if (n_q + n_k + n_v + n_stat > 0x7fffffffLL) return fail(SAGE_ERR_INVALID_ARG, "too many quantisation blocks");
+  if (need_stats) {
+    char* w = static_cast<char*>(ws);
+    p.ksum_part = want_km ? reinterpret_cast<double*>(w) : nullptr;
+    p.vmax_part = want_v ? reinterpret_cast<float*>(w + align256(ws_ksum_bytes(B, Hkv, Skv, D))) : nullptr;
+    p.stat_k = want_km ? 1 : 0;
+    p.stat_v = want_v ? 1 : 0;
+  }
+  // launch A: Q blocks and statistics chunks (and K blocks when K needs no statistics)
+  p.n_q = (int)n_q;
+  p.n_stat = (int)n_stat;
+  p.n_k = want_km ? 0 : (int)n_k;
+  p.n_v = 0;
+  const int64_t grid_a = (int64_t)p.n_q + p.n_stat + p.n_k;
+  if (grid_a > 0) {
+    sage::prepass_kernel<D, T><<<(unsigned)grid_a, sage::kQuantThreads, 0, st>>>(p);
     SAGE_CUDA_TRY(cudaGetLastError());
+  }
+  if (need_stats) {
+    sage::FinalizeParams fp{};
+    fp.ksum_part = p.ksum_part; fp.vmax_part = p.vmax_part; fp.k_mean = k_mean; fp.v_scale = v_scale;
+    fp.Hkv = (int)Hkv; fp.S = (int)Skv; fp.nchunk = nchunk; fp.D = D;
+    sage::kv_finalize_kernel<<<dim3((unsigned)Hkv, (unsigned)B), 128, 0, st>>>(fp);
+    SAGE_CUDA_TRY(cudaGetLastError());
+    // launch B: K blocks that needed the mean, and V blocks
+    p.n_q = 0;
+    p.n_stat = 0;
+    p.n_k = want_km ? (int)n_k : 0;
+    p.n_v = (int)n_v;
+    const int64_t grid_b = (int64_t)p.n_k + p.n_v;
+    if (grid_b > 0) {
+      sage::prepass_kernel<D, T><<<(unsigned)grid_b, sage::kQuantThreads, 0, st>>>(p);
+      SAGE_CUDA_TRY(cudaGetLastError());
+    }
   }
   return SAGE_OK;
 }

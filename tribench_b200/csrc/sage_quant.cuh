@@ -5,7 +5,7 @@
 // kernels/sage_attn/triton_impl.py:7-33, bit for bit):
 //   x     = fp32(in) * mult                 (mult = fp32(sm_scale*1.44269504) for Q, 1 for K)
 //   scale = max_{block} |x| / 127.0f        (IEEE division, whole [BLK, D] block)
-//   y     = x / scale                       (IEEE division, never reciprocal-multiply)
+//   y     = x / scale                       (correctly rounded quotient, see quotient_rn)
 //   y    += (y >= 0 ? 0.5f : -0.5f)         (fp32 add)
 //   q     = trunc(y) as int8                (NaN -> 0, so an all-zero block gives 0s and scale 0)
 // Blocks are 128 rows for Q and 64 rows for K (triton_impl.py:166-173); rows past the
@@ -17,6 +17,11 @@
 // increasing i, thread partials summed in increasing r, chunks summed in increasing
 // order) so that a host restatement reproduces it bit for bit. K is then quantised from
 // fp32(k) - km[d], matching per_block_int8(q, k, km=<fp32 km>) of the reference.
+//
+// Launches. Each launch runs a list of CTA roles (see PrepassParams):
+//   A: Q quantisation + K/V statistics (+ K quantisation when K needs no statistics)
+//   finalize: K mean / V scales from the statistics
+//   B: K quantisation (smoothed) + V to e4m3
 #pragma once
 
 #include "sm100_ptx.cuh"
@@ -26,8 +31,9 @@ namespace sage {
 constexpr int kQuantThreads = 256;
 constexpr int kStatsChunk = 512;  // rows of K/V per statistics CTA
 
-template <typename T> struct Vec8;
-template <> struct Vec8<__half> {
+template <typename T> struct Half8;
+template <> struct Half8<__half> {
+  using H2 = __half2;
   __device__ static __forceinline__ void to_float(const uint4& u, float (&f)[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
@@ -37,8 +43,15 @@ template <> struct Vec8<__half> {
       f[2 * i + 1] = t.y;
     }
   }
+  // max |h| over the 8 halves, exact (comparisons of 16-bit values), as fp32
+  __device__ static __forceinline__ float absmax(const uint4& u) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    __half2 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+    return fmaxf(__low2float(m), __high2float(m));
+  }
 };
-template <> struct Vec8<__nv_bfloat16> {
+template <> struct Half8<__nv_bfloat16> {
+  using H2 = __nv_bfloat162;
   __device__ static __forceinline__ void to_float(const uint4& u, float (&f)[8]) {
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
@@ -47,6 +60,11 @@ template <> struct Vec8<__nv_bfloat16> {
       f[2 * i] = t.x;
       f[2 * i + 1] = t.y;
     }
+  }
+  __device__ static __forceinline__ float absmax(const uint4& u) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    __nv_bfloat162 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+    return fmaxf(__low2float(m), __high2float(m));
   }
 };
 
@@ -70,77 +88,246 @@ __device__ __forceinline__ float block_absmax(float v, float* red) {
   return m;
 }
 
-__device__ __forceinline__ int8_t quant_one(float x, float scale) {
-  float y = __fdiv_rn(x, scale);
-  y = __fadd_rn(y, (y >= 0.0f) ? 0.5f : -0.5f);
-  return static_cast<int8_t>(__float2int_rz(y));
+// Correctly rounded x / s from r = RN(1/s): q0 = RN(x*r) is within a couple of ulps, the
+// residual x - s*q0 is exact in one FMA, and one more FMA q0 + residual*r rounds to the
+// IEEE quotient (Markstein's final-correction step, IBM J. Res. Dev. 34(1), 1990). Used with
+// |x| <= 127*s; s = 0 gives NaN like the IEEE division it replaces.
+__device__ __forceinline__ float quotient_rn(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-s, q0, x);
+  return __fmaf_rn(e, r, q0);
 }
 
-struct StatsParams {
-  const void* k;  // nullptr when not smoothing
-  const void* v;  // nullptr when V is not quantised to FP8
-  int64_t k_sb, k_sh, k_ss, v_sb, v_sh, v_ss;
-  double* ksum_part;   // [B, Hkv, nchunk, D]
-  float* vmax_part;    // [B, Hkv, nchunk, D]
-  int Hkv, S, nchunk;
+__device__ __forceinline__ uint32_t quant_one(float x, float s, float r) {
+  float y = quotient_rn(x, s, r);
+  y = __fadd_rn(y, (y >= 0.0f) ? 0.5f : -0.5f);
+  return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rz(y))));
+}
+
+struct PrepassParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  int64_t q_sb, q_sh, q_ss, k_sb, k_sh, k_ss, v_sb, v_sh, v_ss;
+  int8_t* q_i8;
+  float* q_scale;
+  int8_t* k_i8;
+  float* k_scale;
+  const float* k_mean;  // K quantisation: subtract this channel mean (nullable: no smoothing)
+  uint8_t* v_fp8;
+  const float* v_scale;
+  double* ksum_part;    // statistics: [B, Hkv, nchunk, D]
+  float* vmax_part;     // statistics: [B, Hkv, nchunk, D]
+  float q_mult;
+  int B, Hq, Hkv, Sq, Skv;
+  int nqb, nkb, nvb, nchunk;
+  // CTA roles of this launch, in grid order: Q blocks, statistics chunks, K blocks, V blocks
+  int n_q, n_stat, n_k, n_v;
+  int stat_k, stat_v;   // which statistics the statistics CTAs gather
 };
 
-// Grid (nchunk, Hkv, B). Per chunk of kStatsChunk rows: fp64 column sums of K and fp32
-// column absmax of V.
-template <int D, typename T>
-__global__ void __launch_bounds__(kQuantThreads) kv_stats_kernel(StatsParams p) {
+// ---------------------------------------------------------------- roles
+template <int D, typename T, int BLK>
+__device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta, bool isq, float* red) {
   constexpr int TPR = D / 8;                 // threads per row (8 channels each)
   constexpr int RPP = kQuantThreads / TPR;   // rows per pass
-  __shared__ double sum_red[RPP][D];
-  __shared__ float max_red[RPP][D];
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  constexpr int NP = BLK / RPP;              // passes
+  const int g = threadIdx.x % TPR, r = threadIdx.x / TPR;
+  const int nb = isq ? p.nqb : p.nkb;
+  const int H = isq ? p.Hq : p.Hkv;
+  const int S = isq ? p.Sq : p.Skv;
+  const int blk = cta % nb;
+  const int hh = (cta / nb) % H;
+  const int bb = cta / (nb * H);
+  const char* src = reinterpret_cast<const char*>(isq ? p.q : p.k) +
+                    (bb * (isq ? p.q_sb : p.k_sb) + hh * (isq ? p.q_sh : p.k_sh)) * (int64_t)sizeof(T) + g * 16;
+  const int64_t ss = (isq ? p.q_ss : p.k_ss) * (int64_t)sizeof(T);
+  const int row0 = blk * BLK;
+  const bool smooth = !isq && p.k_mean != nullptr;
+  float km[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) km[i] = 0.0f;
+  if (smooth) {
+    const float* kmp = p.k_mean + ((size_t)bb * p.Hkv + hh) * D + g * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) km[i] = kmp[i];
+  }
+  uint4 raw[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int row = row0 + r + i * RPP;
+    raw[i] = (row < S) ? ldg_nc_v4(src + row * ss) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float amax = 0.0f;
+  if (smooth) {
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      float f[8];
+      Half8<T>::to_float(raw[i], f);
+      const bool in = row0 + r + i * RPP < S;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, in ? fabsf(__fsub_rn(f[e], km[e])) : 0.0f);
+    }
+  } else {
+    // max |in| on the raw 16-bit values; RN(|in| * mult) is monotone in |in|, so this gives
+    // max |x| exactly after one multiplication
+#pragma unroll
+    for (int i = 0; i < NP; ++i) amax = fmaxf(amax, Half8<T>::absmax(raw[i]));
+  }
+  float m = block_absmax(amax, red);
+  if (isq) m = __fmul_rn(m, p.q_mult);
+  const float scale = __fdiv_rn(m, 127.0f);
+  const float rcp = __frcp_rn(scale);
+  const size_t head = (size_t)bb * H + hh;
+  if (threadIdx.x == 0) (isq ? p.q_scale : p.k_scale)[head * nb + blk] = scale;
+  int8_t* dst = (isq ? p.q_i8 : p.k_i8) + head * (size_t)S * D + g * 8;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int row = row0 + r + i * RPP;
+    if (row < S) {
+      float f[8];
+      Half8<T>::to_float(raw[i], f);
+      uint32_t w[2] = {0u, 0u};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float x = f[e];
+        if (smooth) x = __fsub_rn(x, km[e]);
+        if (isq) x = __fmul_rn(x, p.q_mult);
+        w[e >> 2] |= quant_one(x, scale, rcp) << (8 * (e & 3));
+      }
+      *reinterpret_cast<uint2*>(dst + (size_t)row * D) = make_uint2(w[0], w[1]);
+    }
+  }
+}
+
+// Statistics over one chunk of kStatsChunk rows: fp64 column sums of K, fp32 column absmax of V.
+template <int D, typename T>
+__device__ __forceinline__ void stats_role(const PrepassParams& p, int cta, double (*sum_red)[D], float (*max_red)[D]) {
+  constexpr int TPR = D / 8;
+  constexpr int RPP = kQuantThreads / TPR;
+  constexpr int U = 4;  // rows in flight per thread
+  const int c = cta % p.nchunk;
+  const int h = (cta / p.nchunk) % p.Hkv;
+  const int b = cta / (p.nchunk * p.Hkv);
   const int g = threadIdx.x % TPR, r = threadIdx.x / TPR;
   const int row0 = c * kStatsChunk;
-  const int row1 = min(p.S, row0 + kStatsChunk);
+  const int row1 = min(p.Skv, row0 + kStatsChunk);
   double acc[8];
   float amax[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) { acc[i] = 0.0; amax[i] = 0.0f; }
-  const char* kb = p.k ? reinterpret_cast<const char*>(p.k) +
-                             (b * p.k_sb + h * p.k_sh) * (int64_t)sizeof(T) + g * 16
-                       : nullptr;
-  const char* vb = p.v ? reinterpret_cast<const char*>(p.v) +
-                             (b * p.v_sb + h * p.v_sh) * (int64_t)sizeof(T) + g * 16
-                       : nullptr;
-  for (int row = row0 + r; row < row1; row += RPP) {
-    if (kb) {
-      float f[8];
-      Vec8<T>::to_float(ldg_nc_v4(kb + row * p.k_ss * (int64_t)sizeof(T)), f);
+  const char* kb = p.stat_k ? reinterpret_cast<const char*>(p.k) + (b * p.k_sb + h * p.k_sh) * (int64_t)sizeof(T) + g * 16
+                            : nullptr;
+  const char* vb = p.stat_v ? reinterpret_cast<const char*>(p.v) + (b * p.v_sb + h * p.v_sh) * (int64_t)sizeof(T) + g * 16
+                            : nullptr;
+  for (int base = row0 + r; base < row1; base += U * RPP) {
+    uint4 kr[U], vr[U];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = __dadd_rn(acc[i], static_cast<double>(f[i]));
+    for (int u = 0; u < U; ++u) {
+      const int row = base + u * RPP;
+      const bool in = row < row1;
+      kr[u] = (kb && in) ? ldg_nc_v4(kb + row * p.k_ss * (int64_t)sizeof(T)) : make_uint4(0u, 0u, 0u, 0u);
+      vr[u] = (vb && in) ? ldg_nc_v4(vb + row * p.v_ss * (int64_t)sizeof(T)) : make_uint4(0u, 0u, 0u, 0u);
     }
-    if (vb) {
-      float f[8];
-      Vec8<T>::to_float(ldg_nc_v4(vb + row * p.v_ss * (int64_t)sizeof(T)), f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax[i] = fmaxf(amax[i], fabsf(f[i]));
+    for (int u = 0; u < U; ++u) {
+      if (base + u * RPP < row1) {  // rows in increasing order: the fixed summation order
+        if (kb) {
+          float f[8];
+          Half8<T>::to_float(kr[u], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = __dadd_rn(acc[e], static_cast<double>(f[e]));
+        }
+        if (vb) {
+          float f[8];
+          Half8<T>::to_float(vr[u], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) amax[e] = fmaxf(amax[e], fabsf(f[e]));
+        }
+      }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    sum_red[r][g * 8 + i] = acc[i];
-    max_red[r][g * 8 + i] = amax[i];
+  for (int e = 0; e < 8; ++e) {
+    sum_red[r][g * 8 + e] = acc[e];
+    max_red[r][g * 8 + e] = amax[e];
   }
   __syncthreads();
   if (threadIdx.x < D) {
     const int d = threadIdx.x;
     const size_t o = (((size_t)b * p.Hkv + h) * p.nchunk + c) * D + d;
-    if (p.k) {
+    if (kb) {
       double s = 0.0;
       for (int i = 0; i < RPP; ++i) s = __dadd_rn(s, sum_red[i][d]);
       p.ksum_part[o] = s;
     }
-    if (p.v) {
-      float m = 0.0f;
-      for (int i = 0; i < RPP; ++i) m = fmaxf(m, max_red[i][d]);
-      p.vmax_part[o] = m;
+    if (vb) {
+      float mx = 0.0f;
+      for (int i = 0; i < RPP; ++i) mx = fmaxf(mx, max_red[i][d]);
+      p.vmax_part[o] = mx;
     }
   }
+}
+
+// V -> e4m3 with per-channel scales, 64-row blocks: v / v_scale (correctly rounded quotient),
+// then cvt.rn.satfinite; a channel whose scale is 0 gives 0.
+template <int D, typename T>
+__device__ __forceinline__ void vquant_role(const PrepassParams& p, int cta) {
+  constexpr int TPR = D / 8;
+  constexpr int RPP = kQuantThreads / TPR;
+  const int g = threadIdx.x % TPR, r = threadIdx.x / TPR;
+  const int blk = cta % p.nvb;
+  const int hh = (cta / p.nvb) % p.Hkv;
+  const int bb = cta / (p.nvb * p.Hkv);
+  const size_t head = (size_t)bb * p.Hkv + hh;
+  const char* src = reinterpret_cast<const char*>(p.v) + (bb * p.v_sb + hh * p.v_sh) * (int64_t)sizeof(T) + g * 16;
+  float vs[8], rv[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    vs[e] = p.v_scale[head * D + g * 8 + e];
+    rv[e] = __frcp_rn(vs[e]);
+  }
+  uint8_t* dst = p.v_fp8 + head * (size_t)p.Skv * D + g * 8;
+  constexpr int NP = 64 / RPP;
+  uint4 raw[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int row = blk * 64 + r + i * RPP;
+    raw[i] = (row < p.Skv) ? ldg_nc_v4(src + row * p.v_ss * (int64_t)sizeof(T)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int row = blk * 64 + r + i * RPP;
+    if (row >= p.Skv) continue;
+    float f[8];
+    Half8<T>::to_float(raw[i], f);
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const float a = vs[e] > 0.0f ? quotient_rn(f[e], vs[e], rv[e]) : 0.0f;
+      const float c = vs[e + 1] > 0.0f ? quotient_rn(f[e + 1], vs[e + 1], rv[e + 1]) : 0.0f;
+      const __nv_fp8x2_storage_t pr = __nv_cvt_float2_to_fp8x2(make_float2(a, c), __NV_SATFINITE, __NV_E4M3);
+      w[e >> 2] |= static_cast<uint32_t>(pr) << (8 * (e & 3));
+    }
+    *reinterpret_cast<uint2*>(dst + (size_t)row * D) = make_uint2(w[0], w[1]);
+  }
+}
+
+// One launch of the pre-pass: CTA roles in grid order Q blocks | statistics chunks | K blocks | V blocks.
+template <int D, typename T>
+__global__ void __launch_bounds__(kQuantThreads) prepass_kernel(PrepassParams p) {
+  constexpr int RPP = kQuantThreads / (D / 8);
+  __shared__ double sum_red[RPP][D];
+  __shared__ float max_red[RPP][D];
+  __shared__ float red[kQuantThreads / 32];
+  int cta = blockIdx.x;
+  if (cta < p.n_q) { quant_block_role<D, T, 128>(p, cta, true, red); return; }
+  cta -= p.n_q;
+  if (cta < p.n_stat) { stats_role<D, T>(p, cta, sum_red, max_red); return; }
+  cta -= p.n_stat;
+  if (cta < p.n_k) { quant_block_role<D, T, 64>(p, cta, false, red); return; }
+  cta -= p.n_k;
+  vquant_role<D, T>(p, cta);
 }
 
 struct FinalizeParams {
@@ -165,129 +352,6 @@ __global__ void kv_finalize_kernel(FinalizeParams p) {
     float m = 0.0f;
     for (int c = 0; c < p.nchunk; ++c) m = fmaxf(m, p.vmax_part[(head * p.nchunk + c) * p.D + d]);
     p.v_scale[head * p.D + d] = __fdiv_rn(m, 448.0f);
-  }
-}
-
-struct QuantParams {
-  const void* q;
-  const void* k;
-  const void* v;  // FP8 V quantisation (nullable)
-  int64_t q_sb, q_sh, q_ss, k_sb, k_sh, k_ss, v_sb, v_sh, v_ss;
-  int8_t* q_i8;
-  float* q_scale;
-  int8_t* k_i8;
-  float* k_scale;
-  const float* k_mean;  // nullable: smoothing off
-  uint8_t* v_fp8;
-  const float* v_scale;
-  float q_mult;
-  int B, Hq, Hkv, Sq, Skv;
-  int nqb, nkb, nvb;        // blocks per head
-  int n_q_ctas, n_k_ctas;   // CTA ranges: [0,nq) Q, [nq,nq+nk) K, rest V
-};
-
-// One CTA per quantisation block. Blocks of Q come first in the grid, then K, then V.
-template <int D, typename T>
-__global__ void __launch_bounds__(kQuantThreads) quant_kernel(QuantParams p) {
-  constexpr int TPR = D / 8;
-  constexpr int RPP = kQuantThreads / TPR;
-  __shared__ float red[kQuantThreads / 32];
-  const int g = threadIdx.x % TPR, r = threadIdx.x / TPR;
-  int cta = blockIdx.x;
-
-  if (cta < p.n_q_ctas || cta < p.n_q_ctas + p.n_k_ctas) {
-    const bool isq = cta < p.n_q_ctas;
-    if (!isq) cta -= p.n_q_ctas;
-    const int BLK = isq ? 128 : 64;
-    const int nb = isq ? p.nqb : p.nkb;
-    const int H = isq ? p.Hq : p.Hkv;
-    const int S = isq ? p.Sq : p.Skv;
-    const int blk = cta % nb;
-    const int hh = (cta / nb) % H;
-    const int bb = cta / (nb * H);
-    const char* src = reinterpret_cast<const char*>(isq ? p.q : p.k) +
-                      (bb * (isq ? p.q_sb : p.k_sb) + hh * (isq ? p.q_sh : p.k_sh)) *
-                          (int64_t)sizeof(T) +
-                      g * 16;
-    const int64_t ss = (isq ? p.q_ss : p.k_ss) * (int64_t)sizeof(T);
-    const float mult = isq ? p.q_mult : 1.0f;
-    float km[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) km[i] = 0.0f;
-    const bool smooth = !isq && p.k_mean != nullptr;
-    if (smooth) {
-      const float* kmp = p.k_mean + ((size_t)bb * p.Hkv + hh) * D + g * 8;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) km[i] = kmp[i];
-    }
-    constexpr int MAXP = 128 / RPP;  // passes for a 128-row block
-    float x[MAXP][8];
-    float amax = 0.0f;
-    const int row0 = blk * BLK;
-    const int npass = BLK / RPP;
-#pragma unroll
-    for (int i = 0; i < MAXP; ++i) {
-      const int row = row0 + r + i * RPP;
-      if (i < npass && row < S) {
-        float f[8];
-        Vec8<T>::to_float(ldg_nc_v4(src + row * ss), f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          float t = smooth ? __fsub_rn(f[e], km[e]) : f[e];
-          t = isq ? __fmul_rn(t, mult) : t;
-          x[i][e] = t;
-          amax = fmaxf(amax, fabsf(t));
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = 0.0f;
-      }
-    }
-    const float m = block_absmax(amax, red);
-    const float scale = __fdiv_rn(m, 127.0f);
-    const size_t head = (size_t)bb * H + hh;
-    if (threadIdx.x == 0) (isq ? p.q_scale : p.k_scale)[head * nb + blk] = scale;
-    int8_t* dst = (isq ? p.q_i8 : p.k_i8) + head * (size_t)S * D + g * 8;
-#pragma unroll
-    for (int i = 0; i < MAXP; ++i) {
-      const int row = row0 + r + i * RPP;
-      if (i < npass && row < S) {
-        uint32_t w[2] = {0u, 0u};
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          w[e >> 2] |= (static_cast<uint32_t>(static_cast<uint8_t>(quant_one(x[i][e], scale))))
-                       << (8 * (e & 3));
-        *reinterpret_cast<uint2*>(dst + (size_t)row * D) = make_uint2(w[0], w[1]);
-      }
-    }
-    return;
-  }
-
-  // ---- V -> FP8 e4m3 with per-channel scales (64-row blocks).
-  cta -= p.n_q_ctas + p.n_k_ctas;
-  const int blk = cta % p.nvb;
-  const int hh = (cta / p.nvb) % p.Hkv;
-  const int bb = cta / (p.nvb * p.Hkv);
-  const size_t head = (size_t)bb * p.Hkv + hh;
-  const char* src = reinterpret_cast<const char*>(p.v) +
-                    (bb * p.v_sb + hh * p.v_sh) * (int64_t)sizeof(T) + g * 16;
-  float vs[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) vs[e] = p.v_scale[head * D + g * 8 + e];
-  uint8_t* dst = p.v_fp8 + head * (size_t)p.Skv * D + g * 8;
-  for (int row = blk * 64 + r; row < min(p.Skv, blk * 64 + 64); row += RPP) {
-    float f[8];
-    Vec8<T>::to_float(ldg_nc_v4(src + row * p.v_ss * (int64_t)sizeof(T)), f);
-    uint32_t w[2] = {0u, 0u};
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const float a = vs[e] > 0.0f ? __fdiv_rn(f[e], vs[e]) : 0.0f;
-      const float c = vs[e + 1] > 0.0f ? __fdiv_rn(f[e + 1], vs[e + 1]) : 0.0f;
-      const __nv_fp8x2_storage_t pr =
-          __nv_cvt_float2_to_fp8x2(make_float2(a, c), __NV_SATFINITE, __NV_E4M3);
-      w[e >> 2] |= static_cast<uint32_t>(pr) << (8 * (e & 3));
-    }
-    *reinterpret_cast<uint2*>(dst + (size_t)row * D) = make_uint2(w[0], w[1]);
   }
 }
 
