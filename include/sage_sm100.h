@@ -95,6 +95,27 @@ int sage_per_block_int8(const void* q, const void* k, int dtype,
                         float* k_mean, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * sage_per_block_int8 without a workspace argument, for callers that cannot allocate device
+ * memory themselves: code whose device memory is owned by someone else (a host framework or
+ * inference server that hands out only its own buffers), or that must not call cudaMalloc /
+ * cudaFree because those may synchronise the device. The smoothing statistics use a scratch
+ * array compiled into the library (4 MiB, held on every GPU that loads the library until the
+ * process exits); sizes needing more (batch * heads_kv * ceil(seq_kv / 512) * head_dim above
+ * 524288) are rejected with SAGE_ERR_INVALID_ARG. The caller still passes every input and
+ * output. The first call on a device looks up the scratch's device address (no allocation),
+ * so make that first call before any stream capture. Every call on a device shares the one
+ * scratch array: calls that overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller. No counterpart in the reference.
+ */
+int sage_per_block_int8_noalloc(const void* q, const void* k, int dtype,
+                                int64_t batch, int64_t heads_q, int64_t heads_kv,
+                                int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                                const int64_t q_strides[3], const int64_t k_strides[3],
+                                float sm_scale, unsigned flags,
+                                int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale,
+                                float* k_mean, void* stream);
+
+/*
  * Quantise V to FP8 e4m3 with one scale per (batch, head, channel):
  * v_scale = max_s |v| / 448, v_fp8 = e4m3_rn_satfinite(v / v_scale).
  * No counterpart in the reference (its P.V runs in fp16, triton_impl.py:111-113); it is

@@ -115,3 +115,16 @@ def test_error_message_is_cleared_by_next_call():
     assert lib.sage_workspace_bytes(1, 1, 1, 64, 0, 0) == 0
     assert _pbi8(strides=(1024, 1024, 100)) == N.SAGE_ERR_INVALID_ARG
     assert "head_dim" not in lib.sage_last_error().decode()
+
+
+def test_noalloc_rejects_sizes_beyond_its_scratch():
+    """Host-side validation only (no device here): the allocation-free variant refuses sizes
+    whose statistics need more than its built-in 4 MiB scratch, before any CUDA call."""
+    lib = N.load()
+    keep, p = _dummy()
+    s = N.strides3(8 * 128, 8 * 128, 128)
+    # batch * heads_kv * ceil(seq_kv / 512) * head_dim = 128 * 64 * 1 * 128 = 1048576 > 524288
+    rc = lib.sage_per_block_int8_noalloc(p, p, N.SAGE_DTYPE_F16, 128, 64, 64, 8, 8, 128, s, s, ctypes.c_float(0.0),
+                                         N.SAGE_FLAG_SMOOTH_K, p, p, p, p, p, None)
+    assert rc == N.SAGE_ERR_INVALID_ARG
+    assert "scratch" in lib.sage_last_error().decode()

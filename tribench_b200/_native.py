@@ -39,6 +39,8 @@ SIGNATURES = {
     "sage_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I, _U]),
     "sage_per_block_int8": (_I, [_P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _F, _U,
                                  _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "sage_per_block_int8_noalloc": (_I, [_P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _F, _U,
+                                         _P, _P, _P, _P, _P, _P]),
     "sage_quant_v_fp8": (_I, [_P, _I, _I64, _I64, _I64, _I64, _I64P, _P, _P, _P, _SZ, _P]),
     "sage_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I,
                            _I64, _I64, _I64, _I64, _I64, _I64, _P]),

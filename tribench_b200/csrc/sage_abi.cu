@@ -307,6 +307,32 @@ __global__ void watchdog_selftest_kernel(unsigned long long limit_ns) {
   __syncthreads();
 }
 
+// ---------------------------------------------------------------- allocation-free variant
+// Scratch of sage_per_block_int8_noalloc: the fp64 K column partial sums of the smoothing
+// statistics. It lives in the library image, so every GPU that loads the library holds it
+// until the process exits, and no call allocates device memory.
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB = 524288 fp64 partial sums
+static __device__ __align__(256) double g_noalloc_scratch[kNoAllocScratchBytes / sizeof(double)];
+
+// Device address of g_noalloc_scratch on the current device. In host code the symbol is only a
+// host-side stand-in, so the address is looked up once per device (with that device current)
+// and cached; the first call on a device does this lookup.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  static void* addr[kMaxDevices];
+  std::lock_guard<std::mutex> lk(g_mutex);
+  if (!addr[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(SAGE_ERR_CUDA, "cudaGetSymbolAddress(g_noalloc_scratch) failed: %s", cudaGetErrorString(e));
+    addr[dev] = ptr;
+  }
+  *out = addr[dev];
+  return SAGE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -348,6 +374,37 @@ int sage_per_block_int8(const void* q, const void* k, int dtype, int64_t batch, 
   return prepass_dispatch(dtype, head_dim, q, k, nullptr, batch, heads_q, heads_kv, seq_q, seq_kv, q_strides,
                           k_strides, nullptr, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8, q_scale, k_i8,
                           k_scale, k_mean, nullptr, nullptr, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int sage_per_block_int8_noalloc(const void* q, const void* k, int dtype, int64_t batch, int64_t heads_q,
+                                int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                                const int64_t q_strides[3], const int64_t k_strides[3], float sm_scale,
+                                unsigned flags, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale,
+                                float* k_mean, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  if (int rc = check_strides("q", q_strides)) return rc;
+  if (int rc = check_strides("k", k_strides)) return rc;
+  if (!q || !k || !q_i8 || !q_scale || !k_i8 || !k_scale) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(q_i8) || !aligned16(k_i8))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k/q_i8/k_i8 must be 16-byte aligned");
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
+  const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
+  const size_t need = km_given ? 0 : sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_16BIT, flags);
+  if (need > kNoAllocScratchBytes)
+    return fail(SAGE_ERR_INVALID_ARG,
+                "sizes need %zu bytes of statistics scratch; the built-in scratch of "
+                "sage_per_block_int8_noalloc holds %zu (batch*heads_kv*ceil(seq_kv/512)*head_dim <= %zu)",
+                need, kNoAllocScratchBytes, kNoAllocScratchBytes / sizeof(double));
+  if (int rc = check_arch()) return rc;
+  void* scratch = nullptr;
+  if (need) {
+    if (int rc = noalloc_scratch(&scratch)) return rc;
+  }
+  return prepass_dispatch(dtype, head_dim, q, k, nullptr, batch, heads_q, heads_kv, seq_q, seq_kv, q_strides,
+                          k_strides, nullptr, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8, q_scale, k_i8,
+                          k_scale, k_mean, nullptr, nullptr, scratch, static_cast<cudaStream_t>(stream));
 }
 
 int sage_quant_v_fp8(const void* v, int dtype, int64_t batch, int64_t heads_kv, int64_t seq_kv, int64_t head_dim,
