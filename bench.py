@@ -13,6 +13,11 @@ global job at N ranks is the workload with batch N times larger; rank r generate
 processes its own batches (no collective on the data path). value = total ops of all ranks /
 max-over-ranks device time.
 
+The sharded long-context workload "c5" (B=16, H=64, S=32K, causal) scales strongly instead:
+the fixed 1024-head grid is split across the ranks, each rank computes its heads in --waves
+waves, and a step ends when the whole output is assembled on rank 0: every other rank sends
+each finished wave to rank 0 (NCCL point to point) while it computes the next one.
+
 --impl reference times the reference's own algorithm on the host CPU (the reference.py `ref`
 PyTorch path, restated per (batch, head) slice in oracle.ref_attention_torch), one sampled
 head per step, rank 0 only.
@@ -34,6 +39,8 @@ if ROOT not in sys.path:
 
 import torch  # noqa: E402
 
+from tribench_b200 import shard  # noqa: E402
+
 METRIC = "sage_attn TOPS (S=8K, D=128) vs INT8 tensor peak"
 UNIT = "TOPS"
 L2_BYTES = 126 * 1024 * 1024
@@ -49,6 +56,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--waves", type=int, default=4, help="head waves per rank (sharded c5 workload)")
     return ap.parse_args()
 
 
@@ -275,13 +283,26 @@ def main():
         pg = dist
     case = workload_case(args.workload, world)
     B, H, S, D = case["batch_size"], case["num_heads"], case["seq_len"], case["head_dim"]
-    nh_total = B * H
-    lo, hi = rank * nh_total // world, (rank + 1) * nh_total // world
+    strong = case["shard"] == "strong"
+    sd = shard.make_shard(case, rank, world)
+    nh_total, lo, hi = sd.total, sd.lo, sd.hi
     inp = tb.make_inputs(case, dev, seed=case["seed"], dtype=case["dtype"], heads=(lo, hi))
     q, k, v = inp["q"], inp["k"], inp["v"]
     causal, pv = case["causal"], case["pv"]
-    plan = tb.SagePlan(1, hi - lo, hi - lo, S, S, D, q.dtype, dev, pv=pv, smooth_k=True, causal=causal)
-    o = torch.empty_like(q)
+    n_waves = max(1, args.waves) if strong else 1
+    waves = shard.wave_ranges(lo, hi, n_waves)
+    plans = {}
+    for (a, b) in waves:
+        if b - a not in plans:
+            plans[b - a] = tb.SagePlan(1, b - a, b - a, S, S, D, q.dtype, dev, pv=pv, smooth_k=True, causal=causal)
+    plan = plans[waves[0][1] - waves[0][0]]
+    full = None
+    if strong and rank == 0:
+        # the whole job's output lives on rank 0; its own heads are computed straight into it
+        full = torch.empty((1, nh_total, S, D), dtype=q.dtype, device=dev)
+        o = full[:, lo:hi]
+    else:
+        o = torch.empty_like(q)
     est_rank = tb.estimate(dict(case, batch_size=1, num_heads=hi - lo))
     est_total = tb.estimate(case)
     stream = torch.cuda.current_stream(dev)
@@ -293,23 +314,40 @@ def main():
         if pg is not None:
             pg.barrier()
 
-    # one step = pre-pass + attention: the two C calls sage_run makes (sage_prepass, then
-    # sage_attn_fwd), split so that CUDA events bracket the attention kernel
-    def step(ev_mid=None, ev_end=None):
+    # one wave = pre-pass + attention over a range of heads: the two C calls sage_run makes
+    # (sage_prepass, then sage_attn_fwd), split so that CUDA events bracket the attention kernel
+    def wave(a, b, ev=None):
+        i, j = a - lo, b - lo
+        pl = plans[j - i]
+        if ev is not None:
+            ev[0].record(stream)
+        pl.prepass(q[:, i:j], k[:, i:j], v[:, i:j])
+        if ev is not None:
+            ev[1].record(stream)
+        pl.attention(v[:, i:j], o[:, i:j])
+        if ev is not None:
+            ev[2].record(stream)
+
+    # one step = every wave of this rank, then (sharded workload, N > 1) the output gather
+    def step(wave_events=None):
         if flush is not None:
             flush.zero_()
-        plan.prepass(q, k, v)
-        if ev_mid is not None:
-            ev_mid.record(stream)
-        plan.attention(v, o)
-        if ev_end is not None:
-            ev_end.record(stream)
+        it = iter(wave_events) if wave_events is not None else None
 
-    # our kernels per step: K-stats + finalize + quantise, then attention
-    launches_per_step = 4
+        def compute(a, b):
+            wave(a, b, next(it) if it is not None else None)
 
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        if strong and world > 1:
+            shard.gather_to(0, o, sd, full, waves=n_waves, compute=compute, timeout_s=300.0)
+        else:
+            for (a, b) in waves:
+                compute(a, b)
+
+    # our kernels per wave: K-stats + finalize + quantise, then attention
+    launches_per_step = 4 * len(waves)
+
+    evs = [[tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in waves] for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
         time.sleep(0.3)  # let nvidia-smi start before the GPU is loaded
         for _ in range(args.warmup):
@@ -323,15 +361,15 @@ def main():
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
         for i in range(args.steps):
-            evs[i][0].record(stream)
-            step(evs[i][1], evs[i][2])
+            step(evs[i])
+            ends[i].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize(dev)
     barrier()
     total_ms = t_start.elapsed_time(t_end)
-    step_ms = [evs[i][0].elapsed_time(evs[i][2]) for i in range(args.steps)]
-    attn_ms = [evs[i][1].elapsed_time(evs[i][2]) for i in range(args.steps)]
-    pre_ms = [evs[i][0].elapsed_time(evs[i][1]) for i in range(args.steps)]
+    step_ms = [evs[i][0][0].elapsed_time(ends[i]) for i in range(args.steps)]
+    attn_ms = [sum(w[1].elapsed_time(w[2]) for w in evs[i]) for i in range(args.steps)]
+    pre_ms = [sum(w[0].elapsed_time(w[1]) for w in evs[i]) for i in range(args.steps)]
     status = tb.device_status(dev)
     if pg is not None:
         t = torch.tensor([total_ms], device=dev)
@@ -340,7 +378,7 @@ def main():
 
     # ---- end to end through the public API: host (pinned) inputs -> device -> run -> host output
     e2e_ms = None
-    if args.e2e_steps > 0:
+    if args.e2e_steps > 0 and not strong:
         e2e_ms = run_e2e(args, plan, q, k, v, o, dev, stream, barrier, pg)
 
     cpu = None
@@ -386,12 +424,17 @@ def main():
                 "d2h_bytes_per_step": o.numel() * o.element_size(),
                 "ms_per_step": round(e2e_ms / args.e2e_steps, 3)},
             "gpu_launches": launches_per_step * args.steps,
+            "waves_per_rank": len(waves),
             "device_status": status,
         }
+        if strong:
+            line["gather"] = {"dst_rank": 0, "bytes_received_per_step": (nh_total - (hi - lo)) * S * D * q.element_size(),
+                              "overlapped": "each rank sends wave w while computing wave w+1"}
+            line["e2e_note"] = "not measured for the sharded workload (25.8 GB of host inputs per step)"
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    del plan, q, k, v, o
+    del plan, plans, q, k, v, o, full
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()

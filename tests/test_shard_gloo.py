@@ -35,7 +35,13 @@ def _worker(rank, world, port, mode, results):
     try:
         sd = sh.make_shard(CASE, rank, world)
         inp = sh.shard_inputs(CASE, sd, "cpu", seed=3, dtype="fp16")
-        out = torch.empty_like(inp["q"])
+        B, H, S, D = CASE["batch_size"], CASE["num_heads"], CASE["seq_len"], CASE["head_dim"]
+        full = torch.empty(B, H, S, D, dtype=torch.float16) if rank == 0 else None
+        if mode == "alias" and rank == 0:
+            # the destination computes straight into its slice of the full output (no copy)
+            out = full.reshape(1, B * H, S, D)[:, sd.lo:sd.hi]
+        else:
+            out = torch.empty_like(inp["q"])
 
         def compute(a, b):
             i, j = a - sd.lo, b - sd.lo
@@ -43,10 +49,6 @@ def _worker(rank, world, port, mode, results):
 
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 fails before sending its shard")
-        full = None
-        if rank == 0:
-            B, H, S, D = CASE["batch_size"], CASE["num_heads"], CASE["seq_len"], CASE["head_dim"]
-            full = torch.empty(B, H, S, D, dtype=torch.float16)
         got = sh.gather_to(0, out, sd, full, waves=3, compute=compute, timeout_s=5.0)
         if rank == 0:
             ref_in = sh.make_inputs(CASE, "cpu", 3, "fp16")
@@ -103,6 +105,12 @@ def test_wave_ranges():
 
 def test_gather_world2_matches_single_process():
     out = _run("ok")
+    assert out[0] == ("ok", True), out
+    assert out[1][0] == "ok", out
+
+
+def test_gather_into_aliased_destination_slice():
+    out = _run("alias")
     assert out[0] == ("ok", True), out
     assert out[1][0] == "ok", out
 

@@ -58,7 +58,10 @@ def gather_to(dst: int, out_local: torch.Tensor, shard: Shard, full: torch.Tenso
     """Assemble every rank's [1, heads, S, D] output into `full` ([total, S, D] view) on rank `dst`.
 
     `compute(wave_lo, wave_hi)` (optional) fills out_local for one wave of this rank's heads
-    before it is sent, so sends of finished waves overlap the computation of the next.
+    before it is sent, so sends of finished waves overlap the computation of the next. The
+    destination posts all its receives first, one group per wave (the peers' transfers of a
+    wave run concurrently), so they land while it computes its own heads; `out_local` may be
+    the destination's own slice of `full`, which is then not copied.
     Returns `full` on `dst`, None elsewhere. Uses point-to-point send/recv of contiguous head
     slices (works with NCCL on GPUs and gloo on CPUs). Every wait is bounded by `timeout_s`, so a
     rank that never sends (it failed) makes the destination raise instead of hang.
@@ -71,28 +74,28 @@ def gather_to(dst: int, out_local: torch.Tensor, shard: Shard, full: torch.Tenso
 
     rank, world = shard.rank, shard.world
     local = out_local.reshape(shard.heads, *out_local.shape[2:])
-    pending = []
-    for (a, b) in wave_ranges(shard.lo, shard.hi, waves):
-        if compute is not None:
-            compute(a, b)
-        if rank != dst and b > a:
-            pending.append(dist.isend(local[a - shard.lo:b - shard.lo].contiguous(), dst, group=group))
+    reqs = []
+    flat = None
     if rank == dst:
         if full is None:
             raise ValueError("the destination rank needs the `full` output buffer")
         flat = full.reshape(shard.total, *full.shape[-2:])
+        per_rank = [wave_ranges(*head_range(r, world, shard.total), waves) for r in range(world)]
+        for w in range(waves):
+            ops = [dist.P2POp(dist.irecv, flat[a:b], r, group=group)
+                   for r in range(world) if r != dst and w < len(per_rank[r])
+                   for (a, b) in [per_rank[r][w]] if b > a]
+            if ops:
+                reqs.extend(dist.batch_isend_irecv(ops))
+    for (a, b) in wave_ranges(shard.lo, shard.hi, waves):
+        if compute is not None:
+            compute(a, b)
+        if rank != dst and b > a:
+            # a one-op batch: NCCL runs it as plain point to point, not as a serialised collective
+            reqs.extend(dist.batch_isend_irecv(
+                [dist.P2POp(dist.isend, local[a - shard.lo:b - shard.lo].contiguous(), dst, group=group)]))
+    if rank == dst and shard.heads > 0 and local.data_ptr() != flat[shard.lo].data_ptr():
         flat[shard.lo:shard.hi].copy_(local)
-        reqs = []
-        for r in range(world):
-            if r == dst:
-                continue
-            rlo, rhi = head_range(r, world, shard.total)
-            for (a, b) in wave_ranges(rlo, rhi, waves):
-                if b > a:
-                    buf = flat[a:b]
-                    reqs.append(dist.irecv(buf, r, group=group))
-        for q in reqs:
-            q.wait(limit)
-    for q in pending:
+    for q in reqs:
         q.wait(limit)
     return full if rank == dst else None
