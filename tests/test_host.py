@@ -113,3 +113,10 @@ def test_product_does_not_import_oracle():
             if f.endswith(".py"):
                 src = open(os.path.join(dirpath, f)).read()
                 assert "import oracle" not in src and "from oracle" not in src, f
+
+
+def test_host_pipeline_rejects_cpu_device_and_bad_heads():
+    with pytest.raises(ValueError):
+        tb.HostPipeline(1, 4, 4, 128, 128, 64, torch.float16, "cpu")
+    with pytest.raises(ValueError):
+        tb.HostPipeline(1, 6, 4, 128, 128, 64, torch.float16, "cuda:0")

@@ -252,6 +252,90 @@ class SagePlan:
         return out
 
 
+class HostPipeline:
+    """Attention over q/k/v held in host memory, streamed through one GPU in chunks of heads.
+
+    ``pipe.run(q, k, v, out)`` takes contiguous HND host tensors (pinned, for the copies to
+    be asynchronous) and fills ``out`` on the host. The flattened (batch x kv-head) axis is cut
+    into ``chunks`` pieces; each piece goes host -> device on a copy stream, through sage_run
+    (a SagePlan per chunk size) on the caller's current stream, and device -> host on a second
+    copy stream, alternating between two device slots, so the PCIe transfers of one chunk
+    overlap the computation of the next. Every (batch, head) is computed exactly as in one
+    sage_run over the whole tensor, so the output is bit-identical to SagePlan.run. When run()
+    returns, the caller's stream is ordered after the last device -> host copy.
+    """
+
+    def __init__(self, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, dtype, device, *, chunks=8,
+                 pv="16bit", smooth_k=True, causal=False, sm_scale=None):
+        if heads_kv <= 0 or heads_q % heads_kv:
+            raise ValueError(f"heads_q ({heads_q}) must be a multiple of heads_kv ({heads_kv})")
+        self.shape = (batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)
+        self.dtype, self.device = dtype, torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("HostPipeline streams through a CUDA device")
+        self.groups = heads_q // heads_kv
+        n = batch * heads_kv
+        nc = max(1, min(int(chunks), n))
+        self.ranges = [(i * n // nc, (i + 1) * n // nc) for i in range(nc)]
+        self.plans = {}
+        for a, b in self.ranges:
+            m = b - a
+            if m not in self.plans:
+                self.plans[m] = SagePlan(1, m * self.groups, m, seq_q, seq_kv, head_dim, dtype, self.device, pv=pv,
+                                         smooth_k=smooth_k, causal=causal, sm_scale=sm_scale)
+        mmax = max(b - a for a, b in self.ranges)
+        g = self.groups
+        self.slots = [dict(q=torch.empty((1, mmax * g, seq_q, head_dim), dtype=dtype, device=self.device),
+                           k=torch.empty((1, mmax, seq_kv, head_dim), dtype=dtype, device=self.device),
+                           v=torch.empty((1, mmax, seq_kv, head_dim), dtype=dtype, device=self.device),
+                           o=torch.empty((1, mmax * g, seq_q, head_dim), dtype=dtype, device=self.device))
+                      for _ in range(2)]
+        self.h2d = torch.cuda.Stream(self.device)
+        self.d2h = torch.cuda.Stream(self.device)
+
+    def run(self, q, k, v, out):
+        B, Hq, Hkv, Sq, Skv, D = self.shape
+        for name, t, shp in (("q", q, (B, Hq, Sq, D)), ("k", k, (B, Hkv, Skv, D)), ("v", v, (B, Hkv, Skv, D)),
+                             ("out", out, (B, Hq, Sq, D))):
+            if t.device.type != "cpu" or t.dtype != self.dtype or tuple(t.shape) != shp or not t.is_contiguous():
+                raise ValueError(f"{name}: expected a contiguous host tensor of shape {shp} and dtype {self.dtype}")
+        g = self.groups
+        qf, kf, vf, of = (t.view(-1, t.shape[2], D) for t in (q, k, v, out))
+        comp = torch.cuda.current_stream(self.device)
+        # the copy streams start after everything already queued on the caller's stream,
+        # including the previous run() on these slots
+        start = torch.cuda.Event()
+        start.record(comp)
+        self.h2d.wait_event(start)
+        self.d2h.wait_event(start)
+        nc = len(self.ranges)
+        h2d_done = [torch.cuda.Event() for _ in range(nc)]
+        comp_done = [torch.cuda.Event() for _ in range(nc)]
+        d2h_done = [torch.cuda.Event() for _ in range(nc)]
+        for c, (a, b) in enumerate(self.ranges):
+            m = b - a
+            slot = self.slots[c % 2]
+            dq, dk, dv, do = (slot[x][:, : (m * g if x in "qo" else m)] for x in ("q", "k", "v", "o"))
+            with torch.cuda.stream(self.h2d):
+                if c >= 2:
+                    self.h2d.wait_event(comp_done[c - 2])  # the slot's inputs have been consumed
+                dq[0].copy_(qf[a * g:b * g], non_blocking=True)
+                dk[0].copy_(kf[a:b], non_blocking=True)
+                dv[0].copy_(vf[a:b], non_blocking=True)
+                h2d_done[c].record(self.h2d)
+            comp.wait_event(h2d_done[c])
+            if c >= 2:
+                comp.wait_event(d2h_done[c - 2])  # the slot's output has left the device
+            self.plans[m].run(dq, dk, dv, do)
+            comp_done[c].record(comp)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(comp_done[c])
+                of[a * g:b * g].copy_(do[0], non_blocking=True)
+                d2h_done[c].record(self.d2h)
+        comp.wait_event(d2h_done[-1])
+        return out
+
+
 def run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=True, tensor_layout="HND",
                   out=None):
     """Drop-in for run_sage_attn (triton_impl.py:162-200) on sm_100a.
