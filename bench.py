@@ -18,6 +18,9 @@ the fixed 1024-head grid is split across the ranks, each rank computes its heads
 waves, and a step ends when the whole output is assembled on rank 0: every other rank sends
 each finished wave to rank 0 (NCCL point to point) while it computes the next one.
 
+--workload fa_s4k_d64 | fa_s8k_d64 benchmarks the flash_attn pack (fp16 QK^T and P.V, no
+quantisation; its meta.json cases) through sage_flash_attn_fwd, one launch per step.
+
 --impl reference times the reference's own algorithm on the host CPU (the reference.py `ref`
 PyTorch path, restated per (batch, head) slice in oracle.ref_attention_torch), one sampled
 head per step, rank 0 only.
@@ -51,7 +54,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="h8k", choices=["h8k", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="h8k",
+                    choices=["h8k", "c2", "c3", "c4", "c5", "fa_s4k_d64", "fa_s8k_d64"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--e2e-chunks", type=int, default=8, help="head chunks of the host pipeline (e2e)")
@@ -71,7 +75,7 @@ def dist_env():
 def workload_case(name: str, world: int) -> dict:
     import tribench_b200 as tb
 
-    case = dict(tb.CONFIGS[name])
+    case = dict(tb.CONFIGS[name]) if name in tb.CONFIGS else dict(tb.flash_attn.FLASH_CONFIGS[name], pv="16bit")
     case["name"] = name
     case["batch_size_per_rank"] = case["batch_size"]
     if name == "c5":
@@ -204,15 +208,18 @@ def run_reference(args):
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = ops_head * len(times) / total / 1e12
+    flash = args.workload.startswith("fa_")
+    metric = "flash_attn TFLOPS (fp16 QK^T and P.V) vs fp16 tensor peak" if flash else METRIC
+    unit = "TFLOP/s" if flash else UNIT
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
+        "impl": "reference", "metric": metric, "value": round(value, 6), "unit": unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / len(times), 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(case, world),
-        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads, "kind": "port",
                          "sample": f"one (b,h) head of the workload per step (S={case['seq_len']}, "
                                    f"D={case['head_dim']}), reference.py ref in fp32 PyTorch on the host"},
-        "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -266,8 +273,113 @@ def run_e2e(args, case, q, k, v, o, dev, stream, barrier, pg) -> float:
     return e2e_ms
 
 
+def main_flash(args):
+    """The flash_attn pack: one sage_flash_attn_fwd launch per step on resident inputs."""
+    import tribench_b200 as tb
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        pg = dist
+    case = dict(tb.flash_attn.FLASH_CONFIGS[args.workload], name=args.workload, pv="16bit", shard="weak")
+    case["batch_size"] *= world
+    sd = shard.make_shard(case, rank, world)
+    inp = tb.make_inputs(case, dev, seed=case["seed"], dtype=case["dtype"], heads=(sd.lo, sd.hi))
+    q, k, v = inp["q"], inp["k"], inp["v"]
+    o = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+    est_rank = tb.estimate(dict(case, batch_size=1, num_heads=sd.heads))
+    est_total = tb.estimate(case)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        time.sleep(0.3)
+        for _ in range(args.warmup):
+            tb.run_flash_attn(q, k, v, causal=case["causal"], out=o)
+        torch.cuda.synchronize(dev)
+        assert tb.device_status(dev) == 0
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            tb.run_flash_attn(q, k, v, causal=case["causal"], out=o)
+            evs[i][1].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    total_ms = t0.elapsed_time(t1)
+    launch_ms = [a.elapsed_time(b) for a, b in evs]
+    if pg is not None:
+        t = torch.tensor([total_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+    # e2e through the public call with host buffers: inputs up, one launch, output down
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, args.e2e_steps)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        for d, h_ in ((dq, hq), (dk, hk), (dv, hv)):
+            d.copy_(h_, non_blocking=True)
+        ho.copy_(tb.run_flash_attn(dq, dk, dv, causal=case["causal"], out=o), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if pg is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    cpu = cpu_baseline(dict(case, seq_len=case["seq_len"]), args.cpu_baseline_seconds) \
+        if rank == 0 and world == 1 and not args.no_cpu_baseline else None
+    if rank == 0:
+        peaks = read_peaks()
+        bf16 = peaks["bf16_sustained"]
+        value = est_total["ops_alg"] * args.steps / (total_ms * 1e-3) / 1e12
+        achieved = est_rank["ops_alg"] / (statistics.mean(launch_ms) * 1e-3) / 1e12
+        line = {
+            "metric": "flash_attn TFLOPS (fp16 QK^T and P.V) vs fp16 tensor peak", "value": round(value, 2),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4), "p50_ms": round(statistics.median(launch_ms), 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16 QK^T + fp16 P.V (fp32 accumulate, fp32 softmax)",
+            "data": "synthetic (seeded per (batch, head) slab; q, k, v ~ N(0, 1))",
+            "config": config_dict(case, world),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
+                         "frac": round(achieved / bf16, 4), "traffic": None, "kernel": "sage_attn_kernel (FLASH)",
+                         "peak_source": f"{peaks['source']} bf16 sustained (dense fp16/bf16 rate)"},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(est_total["ops_alg"] * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
+                    "d2h_bytes_per_step": o.numel() * o.element_size(),
+                    "ms_per_step": round(e2e_ms / e2e_steps, 3)},
+            "gpu_launches": args.steps,
+        }
+        if cpu is not None:
+            cpu["unit"] = "TFLOP/s"
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload.startswith("fa_"):
+        if args.impl == "reference":
+            return run_reference(args)
+        return main_flash(args)
     if args.impl == "reference":
         return run_reference(args)
     rank, world, local = dist_env()

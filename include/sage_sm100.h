@@ -176,6 +176,22 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype,
              void* stream);
 
 /*
+ * Unquantised attention with the same pipeline, for TriBench's flash_attn pack.
+ * Replaces run_flash_attn(q, k, v, causal, sm_scale) — kernels/flash_attn/triton_impl.py:110-128
+ * (its kernel: :13-108). q/k/v/o fp16 or bf16 (dtype), [batch, heads, seq, head_dim] with
+ * element strides, last dimension contiguous; head_dim 64 or 128; heads_q a multiple of
+ * heads_kv (GQA). O = softmax(Q K^T * sm_scale [causal: key <= query]) V, sm_scale <= 0 meaning
+ * head_dim^-0.5; QK^T and P.V on the tensor cores with fp32 accumulation, P in the input dtype,
+ * softmax in fp32. Allocates nothing; runs on `stream`.
+ */
+int sage_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int dtype,
+                        int64_t batch, int64_t heads_q, int64_t heads_kv,
+                        int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                        const int64_t q_strides[3], const int64_t k_strides[3],
+                        const int64_t v_strides[3], const int64_t o_strides[3],
+                        int causal, float sm_scale, void* stream);
+
+/*
  * Synchronise `stream`, then read and clear the device-side status word of the current
  * device (SAGE_DEV_* bits; 0 = no wait ran out). Returns SAGE_OK, or SAGE_ERR_TIMEOUT
  * when any bit was set, or SAGE_ERR_CUDA.

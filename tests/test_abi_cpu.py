@@ -128,3 +128,23 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
                                          N.SAGE_FLAG_SMOOTH_K, p, p, p, p, p, None)
     assert rc == N.SAGE_ERR_INVALID_ARG
     assert "scratch" in lib.sage_last_error().decode()
+
+
+def test_flash_rejects_bad_arguments_before_any_cuda_call():
+    lib = N.load()
+    keep, p = _dummy()
+    s = N.strides3(8 * 128, 8 * 128, 128)
+    args = lambda **kw: dict(dict(dtype=N.SAGE_DTYPE_F16, B=1, Hq=1, Hkv=1, Sq=8, Skv=8, D=128, causal=0), **kw)
+
+    def call(q=p, **kw):
+        a = args(**kw)
+        return lib.sage_flash_attn_fwd(q, p, p, p, a["dtype"], a["B"], a["Hq"], a["Hkv"], a["Sq"], a["Skv"], a["D"],
+                                       s, s, s, s, a["causal"], 0.0, None)
+
+    assert call(D=96) == N.SAGE_ERR_INVALID_ARG and "head_dim" in lib.sage_last_error().decode()
+    assert call(causal=1, Skv=16) == N.SAGE_ERR_INVALID_ARG and "causal" in lib.sage_last_error().decode()
+    assert call(Hq=3, Hkv=2) == N.SAGE_ERR_INVALID_ARG and "multiple" in lib.sage_last_error().decode()
+    assert call(dtype=5) == N.SAGE_ERR_INVALID_ARG
+    assert call(q=ctypes.c_void_p(p.value + 4)) == N.SAGE_ERR_INVALID_ARG
+    assert "aligned" in lib.sage_last_error().decode()
+    assert call(q=None) == N.SAGE_ERR_INVALID_ARG

@@ -6,7 +6,10 @@ Public API (mirrors kernels/sage_attn/triton_impl.py and reference.py):
   quant_v_fp8(v), attn_fwd(quant, v, causal), SagePlan (preallocated repeated calls)
   HostPipeline (host q/k/v -> host output, PCIe copies overlapped with the computation)
   make_inputs(case, device, seed, dtype), estimate(case)
+  flash_attn.run_flash_attn(q, k, v, causal=False, sm_scale=None): the flash_attn pack (fp16/bf16 QK^T)
 """
+from . import flash_attn
+from .flash_attn import run_flash_attn
 from .inputs import CONFIGS, estimate, make_inputs, prepass_bytes
 from .sage_attn import (HostPipeline, SagePlan, SageQuant, attn_fwd, device_status, per_block_int8, quant_v_fp8,
                         run, run_sage_attn, watchdog_selftest, workspace_bytes)
@@ -14,4 +17,5 @@ from .sage_attn import (HostPipeline, SagePlan, SageQuant, attn_fwd, device_stat
 __all__ = [
     "CONFIGS", "estimate", "make_inputs", "prepass_bytes", "HostPipeline", "SagePlan", "SageQuant", "attn_fwd", "device_status",
     "per_block_int8", "quant_v_fp8", "run", "run_sage_attn", "watchdog_selftest", "workspace_bytes",
+    "flash_attn", "run_flash_attn",
 ]

@@ -48,6 +48,8 @@ SIGNATURES = {
                           _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "sage_run": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _I64P,
                       _I, _F, _I, _U, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "sage_flash_attn_fwd": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _I64P,
+                                 _I, _F, _P]),
     "sage_device_status": (_I, [ctypes.POINTER(ctypes.c_int), _P]),
     "sage_watchdog_selftest": (_I, [_U, _P]),
 }

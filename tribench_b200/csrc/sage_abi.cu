@@ -229,12 +229,12 @@ int prepass_dispatch(int dtype, int64_t D, const void* q, const void* k, const v
 }
 
 // ---------------------------------------------------------------- attention launch
-template <int D, int PV, bool OBF16>
+template <int D, int PV, bool OBF16, bool FLASH = false>
 int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const sage::AttnParams& p,
                 cudaStream_t st) {
   constexpr int QT = 2;
-  using C = sage::AttnCfg<D, PV, QT>;
-  auto kern = sage::sage_attn_kernel<D, PV, QT, OBF16>;
+  using C = sage::AttnCfg<D, PV, QT, FLASH>;
+  auto kern = sage::sage_attn_kernel<D, PV, QT, OBF16, FLASH>;
   if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), C::SMEM_BYTES)) return rc;
   dim3 grid((unsigned)p.n_m_ctas, (unsigned)p.Hq, (unsigned)p.B);
   kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
@@ -284,6 +284,37 @@ int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, cons
                       : launch_attn<64, sage::kPvE4M3, false>(tq, tk, tv, p, st);
   return obf ? launch_attn<64, sage::kPvBF16, true>(tq, tk, tv, p, st)
              : launch_attn<64, sage::kPvF16, false>(tq, tk, tv, p, st);
+}
+
+// flash_attn pack: the same pipeline on fp16/bf16 Q and K (no pre-pass)
+int flash_impl(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v, const int64_t* vs,
+               void* o, const int64_t* os, int dtype, int causal, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+               int64_t Skv, int64_t D, float sm_scale, cudaStream_t st) {
+  const CUtensorMapDataType dt =
+      dtype == SAGE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tq, tk, tv;
+  if (int rc = encode_4d(&tq, dt, 2, q, D, Sq, Hq, B, qs[2], qs[1], qs[0], 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = encode_4d(&tk, dt, 2, k, D, Skv, Hkv, B, ks[2], ks[1], ks[0], 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = encode_4d(&tv, dt, 2, v, D, Skv, Hkv, B, vs[2], vs[1], vs[0], 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  sage::AttnParams p{};
+  p.o = o;
+  p.o_sb = os[0]; p.o_sh = os[1]; p.o_ss = os[2];
+  p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
+  p.groups = (int)(Hq / Hkv);
+  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64);
+  p.causal = causal ? 1 : 0;
+  p.n_m_ctas = (int)cdiv(Sq, 256);
+  p.wait_limit_ns = wait_limit_ns();
+  const double s = sm_scale > 0.0f ? static_cast<double>(sm_scale) : 1.0 / std::sqrt(static_cast<double>(D));
+  p.qk_scale = static_cast<float>(s * 1.4426950408889634);  // exp(x) = exp2(x * log2(e))
+  if (dtype == SAGE_DTYPE_BF16)
+    return D == 128 ? launch_attn<128, sage::kPvBF16, true, true>(tq, tk, tv, p, st)
+                    : launch_attn<64, sage::kPvBF16, true, true>(tq, tk, tv, p, st);
+  return D == 128 ? launch_attn<128, sage::kPvF16, false, true>(tq, tk, tv, p, st)
+                  : launch_attn<64, sage::kPvF16, false, true>(tq, tk, tv, p, st);
 }
 
 float q_multiplier(float sm_scale, int64_t D) {
@@ -529,6 +560,27 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
   return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, v_strides,
                    fp8 ? v_scale : nullptr, o, o_strides, dtype, pv_mode, causal, batch, heads_q, heads_kv, seq_q,
                    seq_kv, head_dim, st);
+}
+
+int sage_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,
+                        int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                        const int64_t q_strides[3], const int64_t k_strides[3], const int64_t v_strides[3],
+                        const int64_t o_strides[3], int causal, float sm_scale, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  if (causal && seq_q != seq_kv)
+    return fail(SAGE_ERR_INVALID_ARG, "causal attention needs seq_q == seq_kv (got %lld, %lld)", (long long)seq_q,
+                (long long)seq_kv);
+  if (int rc = check_strides("q", q_strides)) return rc;
+  if (int rc = check_strides("k", k_strides)) return rc;
+  if (int rc = check_strides("v", v_strides)) return rc;
+  if (int rc = check_strides("o", o_strides)) return rc;
+  if (!q || !k || !v || !o) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o must be 16-byte aligned");
+  if (int rc = check_arch()) return rc;
+  return flash_impl(q, q_strides, k, k_strides, v, v_strides, o, o_strides, dtype, causal, batch, heads_q, heads_kv,
+                    seq_q, seq_kv, head_dim, sm_scale, static_cast<cudaStream_t>(stream));
 }
 
 int sage_device_status(int* status_bits, void* stream) {

@@ -10,6 +10,10 @@
 // causal) excluded. P.V accumulates in fp32 in TMEM (the reference accumulates each
 // 64-key block in fp16, :113).
 //
+// FLASH = true instantiates the same pipeline without quantisation, for the flash_attn pack
+// (kernels/flash_attn/triton_impl.py:13-108): Q and K stay fp16/bf16, QK^T is kind::f16 into fp32
+// scores, and the scale is sm_scale * log2(e) for every key.
+//
 // CTA = QT query tiles of 128 rows that share every K/V tile (QT = 2: 256 query rows).
 // Warp roles:
 //   warps [0, 4*QT)   softmax: warpgroup t owns query tile t; thread i owns TMEM lane i
@@ -40,16 +44,20 @@ struct AttnParams {
   int causal;
   int n_m_ctas;              // CTAs along the query axis
   unsigned long long wait_limit_ns;
+  float qk_scale;            // FLASH only: sm_scale * log2(e)
 };
 
-template <int D, int PV, int QT>
+template <int D, int PV, int QT, bool FLASH = false>
 struct AttnCfg {
+  static_assert(!FLASH || PV != kPvE4M3, "the flash variant keeps P in the input dtype");
   static constexpr int BM = 128;               // query rows per tile
   static constexpr int BN = 128;               // keys per tile
   static constexpr int V_ELT = (PV == kPvE4M3) ? 1 : 2;
-  static constexpr int NS = (D == 128) ? ((PV == kPvE4M3) ? 4 : 3) : 4;  // K/V ring stages
-  static constexpr int Q_TILE = BM * D;        // bytes (int8)
-  static constexpr int K_TILE = BN * D;        // bytes (int8)
+  static constexpr int QK_ELT = FLASH ? 2 : 1; // bytes per Q/K element (int8, or fp16/bf16)
+  // K/V ring stages (shared memory: QT Q tiles + NS x (K + V) tiles within 227 KB)
+  static constexpr int NS = FLASH ? ((D == 128) ? 2 : 4) : ((D == 128) ? ((PV == kPvE4M3) ? 4 : 3) : 4);
+  static constexpr int Q_TILE = BM * D * QK_ELT;  // bytes
+  static constexpr int K_TILE = BN * D * QK_ELT;  // bytes
   static constexpr int V_TILE = BN * D * V_ELT;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + QT * Q_TILE;
@@ -70,9 +78,19 @@ struct AttnCfg {
   static constexpr int REGS_SOFTMAX = 216;
   static constexpr int REGS_OTHER = 72;
   static constexpr int TMEM_COLS = (QT == 2) ? 512 : 256;
-  // K-major operands: SW128 for 128-byte rows, SW64 for 64-byte rows.
-  static constexpr uint32_t QK_LAYOUT = (D == 128) ? kLayoutSW128 : kLayoutSW64;
-  static constexpr uint32_t QK_SBO = (D == 128) ? 1024 : 512;
+  // K-major Q/K: SW64 for 64-byte rows, SW128 for rows of 128 bytes or more, which TMA
+  // splits into 128-byte column atoms of BM (or BN) rows each. Every MMA K-step covers 32 bytes
+  // of a row (32 int8 or 16 fp16/bf16 elements).
+  static constexpr int QK_ROW_BYTES = D * QK_ELT;
+  static constexpr uint32_t QK_LAYOUT = (QK_ROW_BYTES >= 128) ? kLayoutSW128 : kLayoutSW64;
+  static constexpr uint32_t QK_SBO = (QK_ROW_BYTES >= 128) ? 1024 : 512;
+  static constexpr int QK_ATOMS = (QK_ROW_BYTES > 128) ? QK_ROW_BYTES / 128 : 1;
+  static constexpr int QK_BOX = (QK_ROW_BYTES > 128) ? 128 / QK_ELT : D;  // TMA box width, elements
+  static constexpr int QK_STEPS = QK_ROW_BYTES / 32;
+  // byte offset of K-step kk inside a K-major tile of `rows` rows
+  static __device__ __forceinline__ uint32_t qk_step_offset(int kk, int rows) {
+    return (32 * kk / 128) * rows * 128 + (32 * kk) % 128;
+  }
   // V (MN-major B of P.V): rows of D*V_ELT bytes split into 128-byte swizzle atoms.
   static constexpr int V_ROW_BYTES = D * V_ELT;
   static constexpr uint32_t V_LAYOUT = (V_ROW_BYTES >= 128) ? kLayoutSW128 : kLayoutSW64;
@@ -82,9 +100,9 @@ struct AttnCfg {
   static constexpr int V_BOXES = (V_ROW_BYTES > 128) ? V_ROW_BYTES / 128 : 1;
   static constexpr int PV_K = (PV == kPvE4M3) ? 32 : 16;  // keys per P.V MMA
   static constexpr uint32_t P_COL = (PV == kPvE4M3) ? 96 : 64;  // P offset inside S_t
-  static constexpr uint32_t IDESC_QK =
-      make_idesc(kFmtD_S32, kFmtS8, kFmtS8, 0, 0, BM, BN);
   static constexpr uint32_t PV_FMT = (PV == kPvBF16) ? kFmtBF16 : ((PV == kPvE4M3) ? kFmtE4M3 : kFmtF16);
+  static constexpr uint32_t IDESC_QK = FLASH ? make_idesc(kFmtD_F32, PV_FMT, PV_FMT, 0, 0, BM, BN)
+                                             : make_idesc(kFmtD_S32, kFmtS8, kFmtS8, 0, 0, BM, BN);
   static constexpr uint32_t IDESC_PV = make_idesc(kFmtD_F32, PV_FMT, PV_FMT, 0, 1, BM, D);
   // Softmax: the running max is only raised when a tile's max exceeds it by more than LAZY
   // (log2 units), so P = 2^(s - m) <= 2^LAZY and O needs rescaling only on those rare tiles.
@@ -102,11 +120,25 @@ struct AttnCfg {
 // Bounded-wait limit sentinel codes (match SAGE_DEV_* in sage_sm100.h).
 enum : int { kDevTimeoutProducer = 1, kDevTimeoutMma = 2, kDevTimeoutSoftmax = 4, kDevTimeoutEpilogue = 8 };
 
-template <int D, int PV, int QT, bool OBF16>
-__global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
+// QK^T of one query tile against one K tile: S (TMEM) = Q (smem) . K (smem)^T
+template <class C, bool FLASH>
+__device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint32_t k_tile) {
+#pragma unroll
+  for (int kk = 0; kk < C::QK_STEPS; ++kk) {
+    const uint64_t qd = make_smem_desc(q_tile + C::qk_step_offset(kk, C::BM), 16, C::QK_SBO, C::QK_LAYOUT);
+    const uint64_t kd = make_smem_desc(k_tile + C::qk_step_offset(kk, C::BN), 16, C::QK_SBO, C::QK_LAYOUT);
+    if constexpr (FLASH)
+      umma_f16_ss(s_tmem, qd, kd, C::IDESC_QK, kk > 0);
+    else
+      umma_i8_ss(s_tmem, qd, kd, C::IDESC_QK, kk > 0);
+  }
+}
+
+template <int D, int PV, int QT, bool OBF16, bool FLASH>
+__global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  using C = AttnCfg<D, PV, QT>;
+  using C = AttnCfg<D, PV, QT, FLASH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -186,7 +218,10 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
       mbar_arrive_expect_tx(bar_q, QT * C::Q_TILE);
 #pragma unroll
       for (int t = 0; t < QT; ++t)
-        tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE, &tmQ, bar_q, 0, (m_cta * QT + t) * C::BM, h, b);
+#pragma unroll
+        for (int x = 0; x < C::QK_ATOMS; ++x)
+          tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE + x * (C::BM * 128), &tmQ, bar_q, x * C::QK_BOX,
+                      (m_cta * QT + t) * C::BM, h, b);
       for (int j = 0; j < nkv_max; ++j) {
         const int s = j % C::NS;
         SAGE_T_MARK(1)
@@ -195,7 +230,10 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
         }
         SAGE_T_MARK(0)
         mbar_arrive_expect_tx(bar_kfull + s, C::K_TILE);
-        tma_load_4d(smem + C::OFF_K + s * C::K_TILE, &tmK, bar_kfull + s, 0, j * C::BN, hkv, b);
+#pragma unroll
+        for (int x = 0; x < C::QK_ATOMS; ++x)
+          tma_load_4d(smem + C::OFF_K + s * C::K_TILE + x * (C::BN * 128), &tmK, bar_kfull + s, x * C::QK_BOX,
+                      j * C::BN, hkv, b);
         mbar_arrive_expect_tx(bar_vfull + s, C::V_TILE);
 #pragma unroll
         for (int x = 0; x < C::V_BOXES; ++x)
@@ -219,11 +257,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
           if (nkv[t] == 0) continue;
-          const uint64_t qd = make_smem_desc(q_addr + t * C::Q_TILE, 16, C::QK_SBO, C::QK_LAYOUT);
-          const uint64_t kd = make_smem_desc(k_addr, 16, C::QK_SBO, C::QK_LAYOUT);
-#pragma unroll
-          for (int kk = 0; kk < D / 32; ++kk)
-            umma_i8_ss(tmem_base + 256 * t, desc_advance(qd, 32 * kk), desc_advance(kd, 32 * kk), C::IDESC_QK, kk > 0);
+          issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr);
           umma_commit(bar_sfull + t);
         }
       }
@@ -269,11 +303,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
               knext_ready = true;
               tc_fence_after();
             }
-            const uint64_t qd = make_smem_desc(q_addr + t * C::Q_TILE, 16, C::QK_SBO, C::QK_LAYOUT);
-            const uint64_t kd = make_smem_desc(k_addr + s1 * C::K_TILE, 16, C::QK_SBO, C::QK_LAYOUT);
-#pragma unroll
-            for (int kk = 0; kk < D / 32; ++kk)
-              umma_i8_ss(tmem_base + 256 * t, desc_advance(qd, 32 * kk), desc_advance(kd, 32 * kk), C::IDESC_QK, kk > 0);
+            issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE);
             umma_commit(bar_sfull + t);
           }
         }
@@ -305,12 +335,14 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
     const uint32_t s_tmem = tmem_base + lane_base + 256 * t;
     const uint32_t o_tmem = s_tmem + 128;
     const int n = nkv[t];
-    const float qs = (n > 0) ? p.q_scale[((size_t)b * p.Hq + h) * p.nqb + r0 / C::BM] : 0.0f;
-    const float* ksp = p.k_scale + ((size_t)b * p.Hkv + hkv) * p.nkb;
+    const float qs = (!FLASH && n > 0) ? p.q_scale[((size_t)b * p.Hq + h) * p.nqb + r0 / C::BM] : 0.0f;
+    const float* ksp = FLASH ? nullptr : p.k_scale + ((size_t)b * p.Hkv + hkv) * p.nkb;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     SAGE_T_DECL
-    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: bit pattern 0x4B400000 + s for |s| < 2^22
+    // INT8 scores are biased: 1.5 * 2^23 has bit pattern 0x4B400000, and 0x4B400000 + s is the
+    // float 1.5 * 2^23 + s for |s| < 2^22. fp32 scores (FLASH) are used as they are.
+    constexpr float kMagic = FLASH ? 0.0f : 12582912.0f;
     for (int j = 0; j < n; ++j) {
       SAGE_T_MARK(5)
       if (!__all_sync(0xffffffffu, mbar_wait(bar_sfull + t, j & 1, abort_flag, kDevTimeoutSoftmax, p.wait_limit_ns))) { ok = false; break; }
@@ -323,7 +355,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
         // int32 score s -> float 12582912 + s exactly (an integer add instead of a conversion);
         // monotone in s, so maxima can be taken on these biased values.
 #pragma unroll
-        for (int c = 0; c < 128; ++c) b[c] = __uint_as_float(sr[c] + 0x4B400000u);
+        for (int c = 0; c < 128; ++c) b[c] = __uint_as_float(FLASH ? sr[c] : sr[c] + 0x4B400000u);
       }
       SAGE_T_MARK(1)
       const int key0 = j * C::BN;
@@ -348,8 +380,8 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT>::NUM_THREADS, 1)
       const int kb0 = 2 * j;
       // a zero scale (all-zero block) is replaced by FLT_MIN: its scores are exactly 0 either
       // way, and masked -inf entries stay -inf instead of becoming NaN
-      const float sc0 = fmaxf(qs * ksp[kb0], 1.17549435e-38f);
-      const float sc1 = (kb0 + 1 < p.nkb) ? fmaxf(qs * ksp[kb0 + 1], 1.17549435e-38f) : sc0;
+      const float sc0 = FLASH ? p.qk_scale : fmaxf(qs * ksp[kb0], 1.17549435e-38f);
+      const float sc1 = FLASH ? p.qk_scale : ((kb0 + 1 < p.nkb) ? fmaxf(qs * ksp[kb0 + 1], 1.17549435e-38f) : sc0);
       const float tmax = fmaxf((hm[0] - kMagic) * sc0, (hm[1] - kMagic) * sc1);
       const bool upd = tmax > m_run + C::LAZY;
       const float m_new = upd ? tmax : m_run;
