@@ -98,10 +98,24 @@ __device__ __forceinline__ float quotient_rn(float x, float s, float r) {
   return __fmaf_rn(e, r, q0);
 }
 
-__device__ __forceinline__ uint32_t quant_one(float x, float s, float r) {
-  float y = quotient_rn(x, s, r);
-  y = __fadd_rn(y, (y >= 0.0f) ? 0.5f : -0.5f);
-  return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rz(y))));
+// Two INT8 codes as 32-bit integers (only their low bytes are used), with packed f32x2
+// arithmetic (each lane an IEEE operation): y = x / s via Markstein's correction, then
+// y + copysign(0.5, y) — the reference's y + (y >= 0 ? 0.5 : -0.5) for every y, -0.0 and NaN
+// included (both truncate to 0) — then truncation.
+__device__ __forceinline__ void quant_two(float2 x, float2 s, float2 ns, float2 r, int& a, int& b) {
+  const float2 q0 = fmul2(x, r);
+  const float2 e = ffma2(ns, q0, x);
+  const float2 y = ffma2(e, r, q0);
+  const float2 z = fadd2(y, make_float2(copysignf(0.5f, y.x), copysignf(0.5f, y.y)));
+  a = __float2int_rz(z.x);
+  b = __float2int_rz(z.y);
+}
+
+// Low bytes of four integers packed little-endian into one word (three byte permutes).
+__device__ __forceinline__ uint32_t pack4_lo_bytes(int a, int b, int c, int d) {
+  const uint32_t ab = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
+  const uint32_t cd = __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040);
+  return __byte_perm(ab, cd, 0x5410);
 }
 
 struct PrepassParams {
@@ -165,8 +179,13 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
       float f[8];
       Half8<T>::to_float(raw[i], f);
       const bool in = row0 + r + i * RPP < S;
+      if (in) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, in ? fabsf(__fsub_rn(f[e], km[e])) : 0.0f);
+        for (int e = 0; e < 8; e += 2) {
+          const float2 x = fsub2(make_float2(f[e], f[e + 1]), make_float2(km[e], km[e + 1]));
+          amax = fmax3(amax, fabsf(x.x), fabsf(x.y));
+        }
+      }
     }
   } else {
     // max |in| on the raw 16-bit values; RN(|in| * mult) is monotone in |in|, so this gives
@@ -178,6 +197,8 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
   if (isq) m = __fmul_rn(m, p.q_mult);
   const float scale = __fdiv_rn(m, 127.0f);
   const float rcp = __frcp_rn(scale);
+  const float2 s2 = make_float2(scale, scale), ns2 = make_float2(-scale, -scale), r2 = make_float2(rcp, rcp);
+  const float2 mult2 = make_float2(p.q_mult, p.q_mult);
   const size_t head = (size_t)bb * H + hh;
   if (threadIdx.x == 0) (isq ? p.q_scale : p.k_scale)[head * nb + blk] = scale;
   int8_t* dst = (isq ? p.q_i8 : p.k_i8) + head * (size_t)S * D + g * 8;
@@ -187,15 +208,16 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
     if (row < S) {
       float f[8];
       Half8<T>::to_float(raw[i], f);
-      uint32_t w[2] = {0u, 0u};
+      int qv[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float x = f[e];
-        if (smooth) x = __fsub_rn(x, km[e]);
-        if (isq) x = __fmul_rn(x, p.q_mult);
-        w[e >> 2] |= quant_one(x, scale, rcp) << (8 * (e & 3));
+      for (int e = 0; e < 8; e += 2) {
+        float2 x = make_float2(f[e], f[e + 1]);
+        if (smooth) x = fsub2(x, make_float2(km[e], km[e + 1]));
+        if (isq) x = fmul2(x, mult2);
+        quant_two(x, s2, ns2, r2, qv[e], qv[e + 1]);
       }
-      *reinterpret_cast<uint2*>(dst + (size_t)row * D) = make_uint2(w[0], w[1]);
+      *reinterpret_cast<uint2*>(dst + (size_t)row * D) =
+          make_uint2(pack4_lo_bytes(qv[0], qv[1], qv[2], qv[3]), pack4_lo_bytes(qv[4], qv[5], qv[6], qv[7]));
     }
   }
 }
@@ -325,9 +347,11 @@ __global__ void __launch_bounds__(kQuantThreads) prepass_kernel(PrepassParams p)
   cta -= p.n_q;
   if (cta < p.n_stat) { stats_role<D, T>(p, cta, sum_red, max_red); return; }
   cta -= p.n_stat;
-  if (cta < p.n_k) { quant_block_role<D, T, 64>(p, cta, false, red); return; }
+  // K and V blocks run in reverse head order: the statistics CTAs of the previous launch read
+  // the last heads most recently, so their rows are the ones still in L2
+  if (cta < p.n_k) { quant_block_role<D, T, 64>(p, p.n_k - 1 - cta, false, red); return; }
   cta -= p.n_k;
-  vquant_role<D, T>(p, cta);
+  vquant_role<D, T>(p, p.n_v - 1 - cta);
 }
 
 struct FinalizeParams {
