@@ -2,11 +2,11 @@
 
 Runs TriBench's own kernels/sage_attn code — ``per_block_int8`` and ``run_sage_attn`` from
 triton_impl.py under ``TRITON_INTERPRET=1`` (CPU), and ``ref`` from reference.py in fp32 —
-on small seeded inputs, and stores inputs and outputs as fixtures. It needs the reference
-checkout (path in $TRIBENCH_REF, default /root/reference) and is run by hand in the build
-container only; the tests read the committed .npz and never import the reference.
+on small seeded inputs, and stores inputs and outputs as fixtures. It needs a TriBench
+checkout (its path in $TRIBENCH_REF) and is run by hand where one exists; the tests read the
+committed .npz and never import the reference.
 
-    python tests/golden/make_golden.py
+    TRIBENCH_REF=/path/to/TriBench python tests/golden/make_golden.py
 
 Cases (all [B, H, S, D], HND layout):
   c1s      B1 H2 S256 D64  fp16, k = N(0,1) + per-channel N(0,2^2) offset (exercises smoothing)
@@ -29,7 +29,9 @@ import sys
 import numpy as np
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = os.environ.get("TRIBENCH_REF", "/root/reference")
+REF = os.environ.get("TRIBENCH_REF")
+if not REF:
+    sys.exit("set TRIBENCH_REF to a TriBench checkout")
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REF, "kernels", "sage_attn"))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))

@@ -75,9 +75,6 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -269,19 +266,6 @@ __device__ __forceinline__ void tmem_ld128_sync(uint32_t taddr, uint32_t (&r)[12
       : "memory");
 }
 #undef SAGE_R8O
-__device__ __forceinline__ void tmem_ld64_sync(uint32_t taddr, uint32_t (&r)[64]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : SAGE_R8(0), SAGE_R8(8), SAGE_R8(16), SAGE_R8(24), SAGE_R8(32), SAGE_R8(40), SAGE_R8(48),
-        SAGE_R8(56)
-      : "r"(taddr)
-      : "memory");
-}
 #undef SAGE_R8
 
 #define SAGE_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), \
@@ -378,11 +362,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-// Exact int32 -> fp32 for |x| < 2^22 without the conversion pipe: the bit pattern of
-// (1.5 * 2^23 + x) is 0x4B400000 + x, so reinterpret and subtract 1.5 * 2^23.
-__device__ __forceinline__ float i2f_exact22(uint32_t x) {
-  return __uint_as_float(x + 0x4B400000u) - 12582912.0f;
 }
 
 }  // namespace sage
