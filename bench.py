@@ -42,7 +42,7 @@ if ROOT not in sys.path:
 
 import torch  # noqa: E402
 
-from tribench_b200 import shard  # noqa: E402
+from tribench_b200 import shard, timing  # noqa: E402
 
 METRIC = "sage_attn TOPS (S=8K, D=128) vs INT8 tensor peak"
 UNIT = "TOPS"
@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--waves", type=int, default=4, help="head waves per rank (sharded c5 workload)")
+    ap.add_argument("--no-tribench-timing", action="store_true",
+                    help="skip the drop-in run() measured with TriBench's do_bench procedure")
     return ap.parse_args()
 
 
@@ -339,6 +341,14 @@ def main_flash(args):
         t = torch.tensor([e2e_ms], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_ms = float(t.item())
+    tri = None
+    if world == 1 and not args.no_tribench_timing:
+        B_, H_, S_, D_ = case["batch_size"], case["num_heads"], case["seq_len"], case["head_dim"]
+        qv, kv_, vv = (t.view(B_, H_, S_, D_) for t in (q, k, v))
+        lat = timing.do_bench(lambda: tb.run_flash_attn(qv, kv_, vv, causal=case["causal"]), device=dev)
+        tri = timing.summarize(lat, flops=est_total["flops"])
+        tri["call"] = "tribench_b200.run_flash_attn(q, k, v, causal) (the plugin's run; output allocated per call)"
+        tri["timer"] = "do_bench restated without Triton: 256 MB L2 flush per rep, warmup 200 ms, rep 2000 ms"
     cpu = cpu_baseline(dict(case, seq_len=case["seq_len"]), args.cpu_baseline_seconds) \
         if rank == 0 and world == 1 and not args.no_cpu_baseline else None
     if rank == 0:
@@ -364,6 +374,8 @@ def main_flash(args):
                     "ms_per_step": round(e2e_ms / e2e_steps, 3)},
             "gpu_launches": args.steps,
         }
+        if tri is not None:
+            line["tribench_timing"] = {k_: (round(v_, 5) if isinstance(v_, float) else v_) for k_, v_ in tri.items()}
         if cpu is not None:
             cpu["unit"] = "TFLOP/s"
             line["cpu_baseline"] = cpu
@@ -495,6 +507,15 @@ def main():
     if args.e2e_steps > 0 and not strong:
         e2e_ms = run_e2e(args, case, q, k, v, o, dev, stream, barrier, pg)
 
+    # the drop-in run(q, k, v, causal) measured the way `tribench run` measures a variant
+    tri = None
+    if world == 1 and not args.no_tribench_timing:
+        qv, kv_, vv = (t.view(B, H, S, D) for t in (q, k, v)) if not strong else (q, k, v)
+        lat = timing.do_bench(lambda: tb.run(qv, kv_, vv, causal=causal, pv=pv), device=dev)
+        tri = timing.summarize(lat, flops=est_total["flops"])
+        tri["call"] = "tribench_b200.run(q, k, v, causal) (the plugin's run; output allocated per call)"
+        tri["timer"] = "do_bench restated without Triton: 256 MB L2 flush per rep, warmup 200 ms, rep 2000 ms"
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(case, args.cpu_baseline_seconds)
@@ -546,6 +567,8 @@ def main():
             line["gather"] = {"dst_rank": 0, "bytes_received_per_step": (nh_total - (hi - lo)) * S * D * q.element_size(),
                               "overlapped": "each rank sends wave w while computing wave w+1"}
             line["e2e_note"] = "not measured for the sharded workload (25.8 GB of host inputs per step)"
+        if tri is not None:
+            line["tribench_timing"] = {k_: (round(v_, 5) if isinstance(v_, float) else v_) for k_, v_ in tri.items()}
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)

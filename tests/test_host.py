@@ -120,3 +120,21 @@ def test_host_pipeline_rejects_cpu_device_and_bad_heads():
         tb.HostPipeline(1, 4, 4, 128, 128, 64, torch.float16, "cpu")
     with pytest.raises(ValueError):
         tb.HostPipeline(1, 6, 4, 128, 128, 64, torch.float16, "cuda:0")
+
+
+def test_tribench_latency_summary_matches_numpy_definitions():
+    import numpy as np
+
+    from tribench_b200 import timing
+
+    lat = [1.0, 1.2, 0.9, 1.1, 3.0, 1.05, 0.95, 1.0]
+    got = timing.summarize(lat, flops=2e12, nbytes=4e9)
+    a = np.array(lat)
+    for key, q in (("latency_ms_p50", 50), ("latency_ms_p90", 90), ("latency_ms_p95", 95), ("latency_ms_p99", 99)):
+        assert got[key] == pytest.approx(float(np.percentile(a, q)))
+    assert got["latency_ms_std"] == pytest.approx(float(np.std(a)))
+    assert got["latency_ms_mean"] == pytest.approx(float(np.mean(a)))
+    assert got["tail_ratio_p99_p50"] == pytest.approx(float(np.percentile(a, 99) / np.percentile(a, 50)))
+    assert got["jitter_cv"] == pytest.approx(float(np.std(a) / np.mean(a)))
+    assert got["tflops"] == pytest.approx(2e12 / (float(np.percentile(a, 50)) * 1e-3) / 1e12)
+    assert got["gbps"] == pytest.approx(4e9 / (float(np.percentile(a, 50)) * 1e-3) / 1e9)
