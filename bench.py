@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--e2e-chunks", type=int, default=8, help="head chunks of the host pipeline (e2e)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--waves", type=int, default=4, help="head waves per rank (sharded c5 workload)")
+    ap.add_argument("--waves", type=int, default=8, help="head waves per rank (sharded c5 workload)")
     ap.add_argument("--no-tribench-timing", action="store_true",
                     help="skip the drop-in run() measured with TriBench's do_bench procedure")
     return ap.parse_args()

@@ -3,7 +3,8 @@
 Public API (mirrors kernels/sage_attn/triton_impl.py and reference.py):
   run / run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=True)
   per_block_int8(q, k, km=None, BLKQ=128, BLKK=64, sm_scale=None, tensor_layout="HND")
-  quant_v_fp8(v), attn_fwd(quant, v, causal), SagePlan (preallocated repeated calls)
+  quant_v_fp8(v), attn_fwd(quant, v, causal), SagePlan (preallocated repeated calls; cuda_graph()
+  captures one call for single-launch replay)
   HostPipeline (host q/k/v -> host output, PCIe copies overlapped with the computation)
   make_inputs(case, device, seed, dtype), estimate(case)
   flash_attn.run_flash_attn(q, k, v, causal=False, sm_scale=None): the flash_attn pack (fp16/bf16 QK^T)
@@ -11,11 +12,11 @@ Public API (mirrors kernels/sage_attn/triton_impl.py and reference.py):
 from . import flash_attn
 from .flash_attn import run_flash_attn
 from .inputs import CONFIGS, estimate, make_inputs, prepass_bytes
-from .sage_attn import (HostPipeline, SagePlan, SageQuant, attn_fwd, device_status, per_block_int8, quant_v_fp8,
-                        run, run_sage_attn, watchdog_selftest, workspace_bytes)
+from .sage_attn import (HostPipeline, SageGraph, SagePlan, SageQuant, attn_fwd, device_status, per_block_int8,
+                        quant_v_fp8, run, run_sage_attn, watchdog_selftest, workspace_bytes)
 
 __all__ = [
-    "CONFIGS", "estimate", "make_inputs", "prepass_bytes", "HostPipeline", "SagePlan", "SageQuant", "attn_fwd", "device_status",
+    "CONFIGS", "estimate", "make_inputs", "prepass_bytes", "HostPipeline", "SageGraph", "SagePlan", "SageQuant", "attn_fwd", "device_status",
     "per_block_int8", "quant_v_fp8", "run", "run_sage_attn", "watchdog_selftest", "workspace_bytes",
     "flash_attn", "run_flash_attn",
 ]

@@ -226,6 +226,10 @@ class SagePlan:
         return attn_fwd(self.quant, v, self.causal, pv=pv, out_dtype=self.dtype, tensor_layout=tensor_layout,
                         out=out)
 
+    def cuda_graph(self, q, k, v, out, tensor_layout="HND") -> "SageGraph":
+        """Capture run(q, k, v, out) into a CUDA graph (see SageGraph)."""
+        return SageGraph(self, q, k, v, out, tensor_layout=tensor_layout)
+
     def run(self, q, k, v, out=None, tensor_layout="HND"):
         B, Hq, Hkv, Sq, Skv, D = self.shape
         for name, t, h, s in (("q", q, Hq, Sq), ("k", k, Hkv, Skv), ("v", v, Hkv, Skv)):
@@ -250,6 +254,30 @@ class SagePlan:
             _vp(qd.v_scale), _vp(self.ws), self.ws_bytes, _stream_ptr(self.device))
         N.check("sage_run", rc)
         return out
+
+
+class SageGraph:
+    """A CUDA graph of one SagePlan.run on fixed buffers: ``replay()`` reruns all its launches
+    (pre-pass and attention) with a single graph launch. Refill ``q``/``k``/``v`` in place
+    between replays; the result is in ``out``."""
+
+    def __init__(self, plan: "SagePlan", q, k, v, out, tensor_layout="HND"):
+        self.plan, self.q, self.k, self.v, self.out = plan, q, k, v, out
+        dev = plan.device
+        with torch.cuda.device(dev):
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                plan.run(q, k, v, out, tensor_layout=tensor_layout)  # first run: function attributes, lazy init
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                plan.run(q, k, v, out, tensor_layout=tensor_layout)
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
 
 
 class HostPipeline:
