@@ -21,10 +21,13 @@
 //   warp 4*QT + 1     MMA issuer: QK^T (kind::i8 -> int32) and P.V (kind::f16/f8f6f4 -> fp32);
 //                     also allocates / frees TMEM
 // TMEM (columns): tile t has S_t at 256*t (128 int32 columns) and O_t at 256*t + 128 (D fp32
-// columns). P_t (16-bit or e4m3) is written over the upper columns of S_t after the thread has
-// read its whole S row, and feeds the P.V MMA straight from TMEM.
-// MMA order per key tile j: PV_t(j) then QK_t(j+1) for each t; the tensor pipe executes
-// tcgen05.mma in issue order, so QK_t(j+1) cannot overwrite P_t(j) before PV_t(j) read it.
+// columns); P_t (16-bit or e4m3) feeds the P.V MMA straight from TMEM.
+//   D = 128: P_t is written over the upper columns of S_t after the thread has read its whole S
+//     row. MMA order per key tile j: PV_t(j) then QK_t(j+1) for each t; the tensor pipe executes
+//     tcgen05.mma in issue order, so QK_t(j+1) cannot overwrite P_t(j) before PV_t(j) read it.
+//   D = 64: P_t has its own columns (256*t + 192), so QK_t(j+1) is issued as soon as softmax has
+//     read S_t(j) (sload) and runs while softmax works on tile j; softmax in turn waits for
+//     PV_t(j-1) to finish (pvdone) before it writes P_t(j) or rescales O_t.
 #pragma once
 
 #include "sm100_ptx.cuh"
@@ -63,7 +66,8 @@ struct AttnCfg {
   static constexpr int OFF_K = OFF_Q + QT * Q_TILE;
   static constexpr int OFF_V = OFF_K + NS * K_TILE;
   static constexpr int OFF_BAR = OFF_V + NS * V_TILE;
-  static constexpr int NUM_BARS = 1 + 3 * NS + 5 * QT;
+  // q, kfull/vfull/kvempty per stage, sfull/phalf/pfull/odone/sload/pvdone per query tile
+  static constexpr int NUM_BARS = 1 + 3 * NS + 6 * QT;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_USED = OFF_MISC + 16;
   // Pad to > half of the SM's shared memory so that exactly one CTA is resident per SM:
@@ -99,7 +103,9 @@ struct AttnCfg {
   static constexpr int V_ATOM_ROW = (V_ROW_BYTES >= 128) ? 128 : V_ROW_BYTES;  // bytes per key row in an atom
   static constexpr int V_BOXES = (V_ROW_BYTES > 128) ? V_ROW_BYTES / 128 : 1;
   static constexpr int PV_K = (PV == kPvE4M3) ? 32 : 16;  // keys per P.V MMA
-  static constexpr uint32_t P_COL = (PV == kPvE4M3) ? 96 : 64;  // P offset inside S_t
+  // P_t in its own TMEM columns when O leaves room (D = 64), else over the upper half of S_t
+  static constexpr bool SEP_P = (D == 64);
+  static constexpr uint32_t P_COL = SEP_P ? 128 + D : ((PV == kPvE4M3) ? 96 : 64);  // offset in the tile
   static constexpr uint32_t PV_FMT = (PV == kPvBF16) ? kFmtBF16 : ((PV == kPvE4M3) ? kFmtE4M3 : kFmtF16);
   static constexpr uint32_t IDESC_QK = FLASH ? make_idesc(kFmtD_F32, PV_FMT, PV_FMT, 0, 0, BM, BN)
                                              : make_idesc(kFmtD_S32, kFmtS8, kFmtS8, 0, 0, BM, BN);
@@ -150,7 +156,8 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
   uint64_t* bar_phalf = bar_sfull + QT;
   uint64_t* bar_pfull = bar_phalf + QT;
   uint64_t* bar_odone = bar_pfull + QT;
-  uint64_t* bar_turn = bar_odone + QT;  // [tile]: the other tile finished its exponentials
+  uint64_t* bar_sload = bar_odone + QT;  // [tile]: softmax holds S_t(j) in registers (SEP_P)
+  uint64_t* bar_pvdone = bar_sload + QT; // [tile]: PV_t(j) has landed in O_t (SEP_P)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -187,7 +194,8 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
       mbar_init(bar_phalf + t, 128);
       mbar_init(bar_pfull + t, 128);
       mbar_init(bar_odone + t, 1);
-      mbar_init(bar_turn + t, 4);  // one arrival per warp of the other tile
+      mbar_init(bar_sload + t, 128);
+      mbar_init(bar_pvdone + t, 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -263,7 +271,26 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
       }
       for (int j = 0; ok && j < nkv_max; ++j) {
         const int s = j % C::NS;
+        const int s1 = (j + 1) % C::NS;
         bool v_ready = false, knext_ready = false;
+        if constexpr (C::SEP_P) {
+          // the next scores first: S_t(j+1) only needs softmax to have read S_t(j)
+#pragma unroll
+          for (int t = 0; t < QT; ++t) {
+            if (j + 1 >= nkv[t]) continue;
+            SAGE_T_MARK(4)
+            if (!mbar_wait(bar_sload + t, j & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
+            if (!knext_ready) {
+              if (!mbar_wait(bar_kfull + s1, ((j + 1) / C::NS) & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
+              knext_ready = true;
+            }
+            SAGE_T_MARK(3)
+            tc_fence_after();
+            issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE);
+            umma_commit(bar_sfull + t);
+          }
+          if (!ok) break;
+        }
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
           if (j >= nkv[t]) continue;
@@ -294,8 +321,9 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
           }
           if (!ok) break;
           if (j + 1 == nkv[t]) umma_commit(bar_odone + t);  // O_t final once this lands
-          if (j + 1 < nkv[t]) {
-            const int s1 = (j + 1) % C::NS;
+          if constexpr (C::SEP_P) {
+            umma_commit(bar_pvdone + t);  // P_t may be rewritten, O_t rescaled, once this lands
+          } else if (j + 1 < nkv[t]) {
             if (!knext_ready) {
               SAGE_T_MARK(4)
               if (!mbar_wait(bar_kfull + s1, ((j + 1) / C::NS) & 1, abort_flag, kDevTimeoutMma, p.wait_limit_ns)) { ok = false; break; }
@@ -352,6 +380,10 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
       {
         uint32_t sr[128];
         tmem_ld128_sync(s_tmem, sr);
+        if constexpr (C::SEP_P) {
+          tc_fence_before();
+          mbar_arrive(bar_sload + t);  // S_t(j) is in registers: QK_t(j+1) may overwrite it
+        }
         // int32 score s -> float 12582912 + s exactly (an integer add instead of a conversion);
         // monotone in s, so maxima can be taken on these biased values.
 #pragma unroll
@@ -393,17 +425,6 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
       const float cc0 = -fmaf(kMagic, sc0, m_use - C::P_SHIFT);
       const float cc1 = -fmaf(kMagic, sc1, m_use - C::P_SHIFT);
       float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#ifdef SAGE_PINGPONG
-      // Ping-pong: the two query tiles take turns on the exponentials (tile 0 of key tile j,
-      // tile 1 of key tile j, tile 0 of key tile j+1, ...), so one tile's MUFU/FMA work overlaps
-      // the other tile's loads, maxima and MMAs instead of competing with its exponentials.
-      if constexpr (QT == 2) {
-        const int n_other = nkv[t ^ 1];
-        const bool must_wait = (t == 1) ? (j < min(n, n_other)) : (j >= 1 && j < min(n, n_other + 1));
-        if (must_wait &&
-            !__all_sync(0xffffffffu, mbar_wait(bar_turn + t, (t == 1 ? j : j - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.wait_limit_ns))) { ok = false; break; }
-      }
-#endif
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         const float2 scv = h2 ? make_float2(sc1, sc1) : make_float2(sc0, sc0);
@@ -439,6 +460,10 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
           tmem_st_wait();
           tc_fence_before();
           mbar_arrive(bar_phalf + t);
+        } else if (C::SEP_P && j > 0) {
+          // P_t(j-1) must have been read and O_t(j-1) accumulated before P_t(j) / the rescale
+          if (!__all_sync(0xffffffffu, mbar_wait(bar_pvdone + t, (j - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.wait_limit_ns))) { ok = false; break; }
+          tc_fence_after();
         }
         // P over the upper columns of S_t (the whole S row is already in registers)
         if constexpr (PV == kPvE4M3)
@@ -447,7 +472,8 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
           tmem_st32(s_tmem + C::P_COL + 32 * h2, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
         if (h2 == 0 && rescale) {
           // O_t *= alpha before any P.V of this tile is released. PV_t(j-1) has completed:
-          // S_t(j) was issued after it and tcgen05 operations complete in order.
+          // S_t(j) was issued after it and tcgen05 operations complete in order (D = 128), or
+          // pvdone said so above (D = 64).
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 32) {
             uint32_t orow[32];
@@ -459,13 +485,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
         }
         SAGE_T_MARK(3 + h2)
       }
-#ifdef SAGE_PINGPONG
-      if constexpr (QT == 2) {
-        const int n_other = nkv[t ^ 1];
-        const bool give = (t == 0) ? (j < min(n, n_other)) : (j < min(n_other - 1, n));
-        if (give && lane == 0) mbar_arrive(bar_turn + (t ^ 1));
-      }
-#endif
+      if (!ok) break;  // a wait inside the loop above gave up
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar_pfull + t);
