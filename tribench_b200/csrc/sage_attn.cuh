@@ -112,8 +112,9 @@ struct AttnCfg {
   static constexpr uint32_t IDESC_PV = make_idesc(kFmtD_F32, PV_FMT, PV_FMT, 0, 1, BM, D);
   // Softmax: the running max is only raised when a tile's max exceeds it by more than LAZY
   // (log2 units), so P = 2^(s - m) <= 2^LAZY and O needs rescaling only on those rare tiles.
-  // FP8 P keeps the exact max and is scaled by 2^P_SHIFT into the e4m3 range.
-  static constexpr float LAZY = (PV == kPvE4M3) ? 0.0f : 8.0f;
+  // FP8 P is scaled by 2^P_SHIFT into the e4m3 range; its threshold keeps
+  // P <= 2^(P_SHIFT + LAZY) = 2^8.8 ~ 445.7 below e4m3's largest finite value, 448.
+  static constexpr float LAZY = (PV == kPvE4M3) ? 0.8f : 8.0f;
   static constexpr float P_SHIFT = (PV == kPvE4M3) ? 8.0f : 0.0f;
   // Exponentials per 32 columns computed by the FMA-pipe polynomial instead of MUFU.ex2.
 #ifdef SAGE_EMU_PER_32
