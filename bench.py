@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="h8k",
-                    choices=["h8k", "c2", "c3", "c4", "c5", "fa_s4k_d64", "fa_s8k_d64"])
+                    choices=["h8k", "c2", "c3", "c4", "c5", "s4k_d64", "s8k_d64", "fa_s4k_d64", "fa_s8k_d64"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--e2e-chunks", type=int, default=8, help="head chunks of the host pipeline (e2e)")

@@ -65,7 +65,12 @@ struct AttnCfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + QT * Q_TILE;
   static constexpr int OFF_V = OFF_K + NS * K_TILE;
-  static constexpr int OFF_BAR = OFF_V + NS * V_TILE;
+  // D = 64 INT8 scores with FP8 P.V start from a bias block: S = 0x4B400000 + s directly (see
+  // issue_qk). Measured: C4 1.807 -> 1.772 ms; with 16-bit P.V, whose MMAs keep the tensor pipe
+  // busier, the extra copies cost more than the integer adds they save (s4k_d64 0.856 -> 0.875).
+  static constexpr bool PRE_BIAS = (D == 64) && !FLASH && (PV == kPvE4M3);
+  static constexpr int OFF_BIAS = OFF_V + NS * V_TILE;          // 4 KB of 0x4B400000 words
+  static constexpr int OFF_BAR = OFF_BIAS + (PRE_BIAS ? 4096 : 0);
   // q, kfull/vfull/kvempty per stage, sfull/phalf/pfull/odone/sload/pvdone per query tile
   static constexpr int NUM_BARS = 1 + 3 * NS + 6 * QT;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
@@ -127,9 +132,17 @@ struct AttnCfg {
 // Bounded-wait limit sentinel codes (match SAGE_DEV_* in sage_sm100.h).
 enum : int { kDevTimeoutProducer = 1, kDevTimeoutMma = 2, kDevTimeoutSoftmax = 4, kDevTimeoutEpilogue = 8 };
 
-// QK^T of one query tile against one K tile: S (TMEM) = Q (smem) . K (smem)^T
+// QK^T of one query tile against one K tile: S (TMEM) = Q (smem) . K (smem)^T. With PRE_BIAS
+// the S columns are first filled with the word 0x4B400000 (tcgen05.cp from a constant block) and
+// the MMA accumulates onto it, so each int32 score s arrives as the bit pattern of the float
+// 1.5 * 2^23 + s (|s| <= 127^2 * 64 < 2^22), which softmax uses without an integer add.
 template <class C, bool FLASH>
-__device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint32_t k_tile) {
+__device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint32_t k_tile, uint32_t bias_addr) {
+  if constexpr (C::PRE_BIAS) {
+    const uint64_t bd = make_smem_desc(bias_addr, 128, 256, 0);  // any layout: every word is equal
+#pragma unroll
+    for (int c = 0; c < C::BN; c += 8) tmem_cp_128x256b(s_tmem + c, bd);
+  }
 #pragma unroll
   for (int kk = 0; kk < C::QK_STEPS; ++kk) {
     const uint64_t qd = make_smem_desc(q_tile + C::qk_step_offset(kk, C::BM), 16, C::QK_SBO, C::QK_LAYOUT);
@@ -137,7 +150,7 @@ __device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint3
     if constexpr (FLASH)
       umma_f16_ss(s_tmem, qd, kd, C::IDESC_QK, kk > 0);
     else
-      umma_i8_ss(s_tmem, qd, kd, C::IDESC_QK, kk > 0);
+      umma_i8_ss(s_tmem, qd, kd, C::IDESC_QK, (kk > 0 || C::PRE_BIAS) ? 1u : 0u);
   }
 }
 
@@ -210,6 +223,11 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
   }
+  if constexpr (C::PRE_BIAS) {
+    uint32_t* bias = reinterpret_cast<uint32_t*>(smem + C::OFF_BIAS);
+    for (int i = threadIdx.x; i < 1024; i += C::NUM_THREADS) bias[i] = 0x4B400000u;
+    fence_proxy_async_smem();  // visible to tcgen05.cp after the barrier below
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -258,6 +276,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
       const uint32_t k_addr = smem_u32(smem + C::OFF_K);
       const uint32_t v_addr = smem_u32(smem + C::OFF_V);
+      const uint32_t bias_addr = smem_u32(smem + C::OFF_BIAS);
       bool ok = mbar_wait(bar_q, 0, abort_flag, kDevTimeoutMma, p.wait_limit_ns);
       // QK of tile 0 for every query tile.
       if (ok) ok = mbar_wait(bar_kfull, 0, abort_flag, kDevTimeoutMma, p.wait_limit_ns);
@@ -266,7 +285,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
           if (nkv[t] == 0) continue;
-          issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr);
+          issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr, bias_addr);
           umma_commit(bar_sfull + t);
         }
       }
@@ -287,7 +306,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
             }
             SAGE_T_MARK(3)
             tc_fence_after();
-            issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE);
+            issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE, bias_addr);
             umma_commit(bar_sfull + t);
           }
           if (!ok) break;
@@ -332,7 +351,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
               knext_ready = true;
               tc_fence_after();
             }
-            issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE);
+            issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE, bias_addr);
             umma_commit(bar_sfull + t);
           }
         }
@@ -388,7 +407,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
         // int32 score s -> float 12582912 + s exactly (an integer add instead of a conversion);
         // monotone in s, so maxima can be taken on these biased values.
 #pragma unroll
-        for (int c = 0; c < 128; ++c) b[c] = __uint_as_float(FLASH ? sr[c] : sr[c] + 0x4B400000u);
+        for (int c = 0; c < 128; ++c) b[c] = __uint_as_float((FLASH || C::PRE_BIAS) ? sr[c] : sr[c] + 0x4B400000u);
       }
       SAGE_T_MARK(1)
       const int key0 = j * C::BN;

@@ -156,6 +156,15 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
           smem_u32(bar))
       : "memory");
 }
+// TMEM (128 lanes x 8 columns of 32 bits) <- shared memory (128 rows x 32 bytes, `desc`). Issued
+// by the MMA thread; executes in order with the tcgen05.mma it issues afterwards.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+}
+// Orders this thread's shared-memory writes before later async-proxy (TMA / tcgen05) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // D(tmem, int32) (+)= A(smem, s8) * B(smem, s8)^T
 __device__ __forceinline__ void umma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                            uint32_t idesc, uint32_t accumulate) {

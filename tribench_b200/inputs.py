@@ -33,6 +33,12 @@ CONFIGS = {
                seed=3, dist="vchan", k_offset_std=2.0),
     "c5": dict(batch_size=16, num_heads=64, seq_len=32768, head_dim=128, causal=True, dtype="fp16", pv="16bit",
                seed=4, dist="studentt", k_offset_std=3.0),
+    # the sage_attn pack's own benchmark cases (kernels/sage_attn/meta.json:25-39), with q, k, v
+    # ~ N(0, 1) as its make_inputs draws them (reference.py:4-13)
+    "s4k_d64": dict(batch_size=8, num_heads=16, seq_len=4096, head_dim=64, causal=False, dtype="fp16", pv="16bit",
+                    seed=7, dist="normal"),
+    "s8k_d64": dict(batch_size=4, num_heads=16, seq_len=8192, head_dim=64, causal=False, dtype="fp16", pv="16bit",
+                    seed=8, dist="normal"),
 }
 
 _TORCH_DTYPES = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32}
