@@ -65,10 +65,11 @@ struct AttnCfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + QT * Q_TILE;
   static constexpr int OFF_V = OFF_K + NS * K_TILE;
-  // D = 64 INT8 scores with FP8 P.V start from a bias block: S = 0x4B400000 + s directly (see
-  // issue_qk). Measured: C4 1.807 -> 1.772 ms; with 16-bit P.V, whose MMAs keep the tensor pipe
-  // busier, the extra copies cost more than the integer adds they save (s4k_d64 0.856 -> 0.875).
-  static constexpr bool PRE_BIAS = (D == 64) && !FLASH && (PV == kPvE4M3);
+  // D = 64 INT8 scores start from a bias block: S = 0x4B400000 + s directly (see issue_qk).
+  // The copy shape follows the measurements: with 16-bit P.V, whose MMAs keep the tensor pipe
+  // busier, the broadcasting 32x128b.warpx4 copy (s8k_d64 1.618 -> 1.587 ms; 128x256b made it
+  // slower); with FP8 P.V the 128x256b copy (C4 1.807 -> 1.772 ms).
+  static constexpr bool PRE_BIAS = (D == 64) && !FLASH;
   static constexpr int OFF_BIAS = OFF_V + NS * V_TILE;          // 4 KB of 0x4B400000 words
   static constexpr int OFF_BAR = OFF_BIAS + (PRE_BIAS ? 4096 : 0);
   // q, kfull/vfull/kvempty per stage, sfull/phalf/pfull/odone/sload/pvdone per query tile
@@ -111,6 +112,7 @@ struct AttnCfg {
   // P_t in its own TMEM columns when O leaves room (D = 64), else over the upper half of S_t
   static constexpr bool SEP_P = (D == 64);
   static constexpr uint32_t P_COL = SEP_P ? 128 + D : ((PV == kPvE4M3) ? 96 : 64);  // offset in the tile
+  static constexpr bool PV_FP8 = (PV == kPvE4M3);
   static constexpr uint32_t PV_FMT = (PV == kPvBF16) ? kFmtBF16 : ((PV == kPvE4M3) ? kFmtE4M3 : kFmtF16);
   static constexpr uint32_t IDESC_QK = FLASH ? make_idesc(kFmtD_F32, PV_FMT, PV_FMT, 0, 0, BM, BN)
                                              : make_idesc(kFmtD_S32, kFmtS8, kFmtS8, 0, 0, BM, BN);
@@ -140,8 +142,13 @@ template <class C, bool FLASH>
 __device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint32_t k_tile, uint32_t bias_addr) {
   if constexpr (C::PRE_BIAS) {
     const uint64_t bd = make_smem_desc(bias_addr, 128, 256, 0);  // any layout: every word is equal
+    if constexpr (C::PV_FP8) {
 #pragma unroll
-    for (int c = 0; c < C::BN; c += 8) tmem_cp_128x256b(s_tmem + c, bd);
+      for (int c = 0; c < C::BN; c += 8) tmem_cp_128x256b(s_tmem + c, bd);
+    } else {
+#pragma unroll
+      for (int c = 0; c < C::BN; c += 4) tmem_cp_32x128b_warpx4(s_tmem + c, bd);
+    }
   }
 #pragma unroll
   for (int kk = 0; kk < C::QK_STEPS; ++kk) {

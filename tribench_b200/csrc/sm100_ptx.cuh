@@ -161,6 +161,11 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t desc) {
   asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
 }
+// TMEM (4 x 32 lanes x 4 columns) <- shared memory (32 rows x 16 bytes, `desc`), the 32 rows
+// broadcast to the four lane quadrants (a quarter of the shared-memory reads of 128x256b).
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+}
 // Orders this thread's shared-memory writes before later async-proxy (TMA / tcgen05) reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
