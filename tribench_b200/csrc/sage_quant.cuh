@@ -30,6 +30,10 @@ namespace sage {
 
 constexpr int kQuantThreads = 256;
 constexpr int kStatsChunk = 512;  // rows of K/V per statistics CTA
+// Scale blocks per quantisation CTA: at D = 64 a block holds half the bytes, so a CTA takes
+// several, keeping eight 16-byte loads per thread in flight as at D = 128.
+template <int D> constexpr int kQBlocksPerCta = (D == 64) ? 2 : 1;
+template <int D> constexpr int kKBlocksPerCta = (D == 64) ? 4 : 1;
 
 template <typename T> struct Half8;
 template <> struct Half8<__half> {
@@ -76,16 +80,26 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   return r;
 }
 
-__device__ __forceinline__ float block_absmax(float v, float* red) {
+// Block-wide maxima of N values per thread in one reduction round; red holds
+// N * (kQuantThreads / 32) floats. Called once per CTA.
+template <int N>
+__device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
+  constexpr int W = kQuantThreads / 32;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) red[w] = v;
+  for (int n = 0; n < N; ++n)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v[n] = fmaxf(v[n], __shfl_xor_sync(0xffffffffu, v[n], o));
+  if ((threadIdx.x & 31) == 0)
+#pragma unroll
+    for (int n = 0; n < N; ++n) red[n * W + (threadIdx.x >> 5)] = v[n];
   __syncthreads();
-  float m = red[0];
 #pragma unroll
-  for (int i = 1; i < kQuantThreads / 32; ++i) m = fmaxf(m, red[i]);
-  return m;
+  for (int n = 0; n < N; ++n) {
+    float m = red[n * W];
+#pragma unroll
+    for (int i = 1; i < W; ++i) m = fmaxf(m, red[n * W + i]);
+    v[n] = m;
+  }
 }
 
 // Correctly rounded x / s from r = RN(1/s): q0 = RN(x*r) is within a couple of ulps, the
@@ -141,22 +155,25 @@ struct PrepassParams {
 };
 
 // ---------------------------------------------------------------- roles
-template <int D, typename T, int BLK>
+// NSUB consecutive scale blocks of BLK rows, all rows loaded up front.
+template <int D, typename T, int BLK, int NSUB>
 __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta, bool isq, float* red) {
   constexpr int TPR = D / 8;                 // threads per row (8 channels each)
   constexpr int RPP = kQuantThreads / TPR;   // rows per pass
-  constexpr int NP = BLK / RPP;              // passes
+  constexpr int PPB = BLK / RPP;             // passes per scale block
+  constexpr int NP = NSUB * PPB;             // passes
   const int g = threadIdx.x % TPR, r = threadIdx.x / TPR;
   const int nb = isq ? p.nqb : p.nkb;
+  const int ng = (nb + NSUB - 1) / NSUB;     // CTAs per head
   const int H = isq ? p.Hq : p.Hkv;
   const int S = isq ? p.Sq : p.Skv;
-  const int blk = cta % nb;
-  const int hh = (cta / nb) % H;
-  const int bb = cta / (nb * H);
+  const int grp = cta % ng;
+  const int hh = (cta / ng) % H;
+  const int bb = cta / (ng * H);
   const char* src = reinterpret_cast<const char*>(isq ? p.q : p.k) +
                     (bb * (isq ? p.q_sb : p.k_sb) + hh * (isq ? p.q_sh : p.k_sh)) * (int64_t)sizeof(T) + g * 16;
   const int64_t ss = (isq ? p.q_ss : p.k_ss) * (int64_t)sizeof(T);
-  const int row0 = blk * BLK;
+  const int row0 = grp * NSUB * BLK;
   const bool smooth = !isq && p.k_mean != nullptr;
   float km[8];
 #pragma unroll
@@ -172,7 +189,9 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
     const int row = row0 + r + i * RPP;
     raw[i] = (row < S) ? ldg_nc_v4(src + row * ss) : make_uint4(0u, 0u, 0u, 0u);
   }
-  float amax = 0.0f;
+  float amax[NSUB];
+#pragma unroll
+  for (int b = 0; b < NSUB; ++b) amax[b] = 0.0f;
   if (smooth) {
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
@@ -183,7 +202,7 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
           const float2 x = fsub2(make_float2(f[e], f[e + 1]), make_float2(km[e], km[e + 1]));
-          amax = fmax3(amax, fabsf(x.x), fabsf(x.y));
+          amax[i / PPB] = fmax3(amax[i / PPB], fabsf(x.x), fabsf(x.y));
         }
       }
     }
@@ -191,20 +210,27 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
     // max |in| on the raw 16-bit values; RN(|in| * mult) is monotone in |in|, so this gives
     // max |x| exactly after one multiplication
 #pragma unroll
-    for (int i = 0; i < NP; ++i) amax = fmaxf(amax, Half8<T>::absmax(raw[i]));
+    for (int i = 0; i < NP; ++i) amax[i / PPB] = fmaxf(amax[i / PPB], Half8<T>::absmax(raw[i]));
   }
-  float m = block_absmax(amax, red);
-  if (isq) m = __fmul_rn(m, p.q_mult);
-  const float scale = __fdiv_rn(m, 127.0f);
-  const float rcp = __frcp_rn(scale);
-  const float2 s2 = make_float2(scale, scale), ns2 = make_float2(-scale, -scale), r2 = make_float2(rcp, rcp);
+  block_max_n<NSUB>(amax, red);
+  float scale[NSUB], rcp[NSUB];
+#pragma unroll
+  for (int b = 0; b < NSUB; ++b) {
+    const float m = isq ? __fmul_rn(amax[b], p.q_mult) : amax[b];
+    scale[b] = __fdiv_rn(m, 127.0f);
+    rcp[b] = __frcp_rn(scale[b]);
+  }
   const float2 mult2 = make_float2(p.q_mult, p.q_mult);
   const size_t head = (size_t)bb * H + hh;
-  if (threadIdx.x == 0) (isq ? p.q_scale : p.k_scale)[head * nb + blk] = scale;
+#pragma unroll
+  for (int b = 0; b < NSUB; ++b)
+    if (threadIdx.x == b && grp * NSUB + b < nb) (isq ? p.q_scale : p.k_scale)[head * nb + grp * NSUB + b] = scale[b];
   int8_t* dst = (isq ? p.q_i8 : p.k_i8) + head * (size_t)S * D + g * 8;
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const int row = row0 + r + i * RPP;
+    const float sc = scale[i / PPB], rc = rcp[i / PPB];
+    const float2 s2 = make_float2(sc, sc), ns2 = make_float2(-sc, -sc), r2 = make_float2(rc, rc);
     if (row < S) {
       float f[8];
       Half8<T>::to_float(raw[i], f);
@@ -341,15 +367,15 @@ __global__ void __launch_bounds__(kQuantThreads) prepass_kernel(PrepassParams p)
   constexpr int RPP = kQuantThreads / (D / 8);
   __shared__ double sum_red[RPP][D];
   __shared__ float max_red[RPP][D];
-  __shared__ float red[kQuantThreads / 32];
+  __shared__ float red[4 * (kQuantThreads / 32)];
   int cta = blockIdx.x;
-  if (cta < p.n_q) { quant_block_role<D, T, 128>(p, cta, true, red); return; }
+  if (cta < p.n_q) { quant_block_role<D, T, 128, kQBlocksPerCta<D>>(p, cta, true, red); return; }
   cta -= p.n_q;
   if (cta < p.n_stat) { stats_role<D, T>(p, cta, sum_red, max_red); return; }
   cta -= p.n_stat;
   // K and V blocks run in reverse head order: the statistics CTAs of the previous launch read
   // the last heads most recently, so their rows are the ones still in L2
-  if (cta < p.n_k) { quant_block_role<D, T, 64>(p, p.n_k - 1 - cta, false, red); return; }
+  if (cta < p.n_k) { quant_block_role<D, T, 64, kKBlocksPerCta<D>>(p, p.n_k - 1 - cta, false, red); return; }
   cta -= p.n_k;
   vquant_role<D, T>(p, p.n_v - 1 - cta);
 }
