@@ -166,7 +166,7 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
   p.v_fp8 = v_fp8; p.v_scale = v_scale;
   p.q_mult = q_mult;
   p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
-  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, 64); p.nchunk = nchunk;
+  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, sage::kVRowsPerCta<D>); p.nchunk = nchunk;
   const int64_t n_q = q ? B * Hq * cdiv(p.nqb, sage::kQBlocksPerCta<D>) : 0;
   const int64_t n_k = k ? B * Hkv * cdiv(p.nkb, sage::kKBlocksPerCta<D>) : 0;
   const int64_t n_v = want_v ? B * Hkv * p.nvb : 0;

@@ -34,6 +34,8 @@ constexpr int kStatsChunk = 512;  // rows of K/V per statistics CTA
 // several, keeping eight 16-byte loads per thread in flight as at D = 128.
 template <int D> constexpr int kQBlocksPerCta = (D == 64) ? 2 : 1;
 template <int D> constexpr int kKBlocksPerCta = (D == 64) ? 4 : 1;
+// Rows of V per e4m3 CTA: eight passes of the CTA's threads (V needs no per-block reduction).
+template <int D> constexpr int kVRowsPerCta = 8 * (kQuantThreads / (D / 8));
 
 template <typename T> struct Half8;
 template <> struct Half8<__half> {
@@ -317,7 +319,7 @@ __device__ __forceinline__ void stats_role(const PrepassParams& p, int cta, doub
   }
 }
 
-// V -> e4m3 with per-channel scales, 64-row blocks: v / v_scale (correctly rounded quotient),
+// V -> e4m3 with per-channel scales, kVRowsPerCta rows per CTA: v / v_scale (correctly rounded quotient),
 // then cvt.rn.satfinite; a channel whose scale is 0 gives 0.
 template <int D, typename T>
 __device__ __forceinline__ void vquant_role(const PrepassParams& p, int cta) {
@@ -336,16 +338,16 @@ __device__ __forceinline__ void vquant_role(const PrepassParams& p, int cta) {
     rv[e] = __frcp_rn(vs[e]);
   }
   uint8_t* dst = p.v_fp8 + head * (size_t)p.Skv * D + g * 8;
-  constexpr int NP = 64 / RPP;
+  constexpr int NP = kVRowsPerCta<D> / RPP;
   uint4 raw[NP];
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
-    const int row = blk * 64 + r + i * RPP;
+    const int row = blk * kVRowsPerCta<D> + r + i * RPP;
     raw[i] = (row < p.Skv) ? ldg_nc_v4(src + row * p.v_ss * (int64_t)sizeof(T)) : make_uint4(0u, 0u, 0u, 0u);
   }
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
-    const int row = blk * 64 + r + i * RPP;
+    const int row = blk * kVRowsPerCta<D> + r + i * RPP;
     if (row >= p.Skv) continue;
     float f[8];
     Half8<T>::to_float(raw[i], f);
