@@ -92,3 +92,15 @@ def test_flash_deterministic():
     a = tb.run_flash_attn(q, k, v, causal=True)
     b = tb.run_flash_attn(q, k, v, causal=True)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("Sq,Skv,D,causal", [(1, 1, 64, False), (17, 17, 128, True), (300, 777, 64, False),
+                                             (1000, 129, 128, False)])
+def test_flash_tiny_and_cross_lengths(Sq, Skv, D, causal):
+    g = torch.Generator(device=DEV).manual_seed(Sq * 7 + Skv)
+    q = torch.randn(1, 2, Sq, D, generator=g, device=DEV).half()
+    k = torch.randn(1, 2, Skv, D, generator=g, device=DEV).half()
+    v = torch.randn(1, 2, Skv, D, generator=g, device=DEV).half()
+    o = tb.run_flash_attn(q, k, v, causal=causal)
+    assert tb.device_status(DEV) == 0
+    assert (o.float() - ref_fp32(q, k, v, causal)).abs().max().item() <= 4e-3

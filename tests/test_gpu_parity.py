@@ -352,3 +352,19 @@ def test_quant_full_size_c2_heads_bit_exact():
         np.testing.assert_array_equal(qs[b:b + 1, h:h + 1].cpu().numpy(), qs_o)
         np.testing.assert_array_equal(ki[b:b + 1, h:h + 1].cpu().numpy(), ki_o)
         np.testing.assert_array_equal(ks[b:b + 1, h:h + 1].cpu().numpy(), ks_o)
+
+
+@pytest.mark.parametrize("Sq,Skv,D", [(300, 777, 128), (1000, 129, 64), (1, 2048, 64)])
+def test_attention_cross_lengths(Sq, Skv, D):
+    """seq_q != seq_kv (non-causal): every query attends to all seq_kv keys."""
+    g = torch.Generator(device=DEV).manual_seed(Sq + Skv)
+    q = torch.randn(1, 2, Sq, D, generator=g, device=DEV).half()
+    k = (torch.randn(1, 2, Skv, D, generator=g, device=DEV) + 2.0 * torch.randn(1, 1, 1, D, generator=g, device=DEV)).half()
+    v = torch.randn(1, 2, Skv, D, generator=g, device=DEV).half()
+    o = f32(tb.run(q, k, v))
+    no_timeout()
+    model = _model_for(q, k, v, False, smooth=True)
+    ref = oracle.ref_attention(f32(q), f32(k), f32(v))
+    assert o.shape == (1, 2, Sq, D)
+    assert np.abs(o - model).max() <= 4e-3
+    assert cos(o, ref) >= 0.999
