@@ -192,6 +192,52 @@ int sage_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, in
                         int causal, float sm_scale, void* stream);
 
 /*
+ * Variable-length batches (packed sequences). `batch` sequences of different lengths are packed
+ * along one token axis, flash-attention style: q is [total_q, heads_q, head_dim] (any head and
+ * token strides, head_dim contiguous), k/v are [total_kv, heads_kv, head_dim], and sequence b
+ * owns token rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) of q / o and [cu_seqlens_kv[b],
+ * cu_seqlens_kv[b+1]) of k / v. cu_seqlens_* are int32 DEVICE arrays of batch + 1 prefix sums
+ * starting at 0; max_seq_q / max_seq_kv bound every sequence's length (the launches are sized
+ * from them; the kernels clamp a longer or malformed sequence to these bounds and to the token
+ * counts, so no access leaves the buffers). Strides are {head, token} element strides.
+ * Every sequence is quantised and attended on its own, exactly as a dense batch of one:
+ * Q blocks of 128 rows and K blocks of 64 rows start at each sequence's first token, and the
+ * smoothing mean is per (sequence, head). Packed intermediates and per-sequence scales:
+ *   q_i8    int8  [heads_q,  total_q,  head_dim]   q_scale fp32 [batch, heads_q,  ceil(max_seq_q/128)]
+ *   k_i8    int8  [heads_kv, total_kv, head_dim]   k_scale fp32 [batch, heads_kv, ceil(max_seq_kv/64)]
+ *   k_mean  fp32  [batch, heads_kv, head_dim]
+ *   v_fp8   e4m3  [heads_kv, total_kv, head_dim]   v_scale fp32 [batch, heads_kv, head_dim]
+ * Scale entries past a sequence's own block count are not written. A sequence with query rows
+ * but no keys gets O = 0 (softmax over an empty key set in the reference's matmuls). causal
+ * masks key j of a sequence for its query i iff j > i (lengths should match per sequence).
+ * Workspace: sage_workspace_bytes(batch, heads_kv, max_seq_kv, head_dim, pv_mode, flags).
+ * The reference has no packed-sequence entry point; these extend per_block_int8 and
+ * run_sage_attn (kernels/sage_attn/triton_impl.py:35-82, :162-200) and run_flash_attn
+ * (kernels/flash_attn/triton_impl.py:110-128) to packed batches, one sequence at a time.
+ */
+int sage_per_block_int8_varlen(const void* q, const void* k, int dtype, int64_t batch, int64_t heads_q,
+                               int64_t heads_kv, int64_t total_q, int64_t total_kv, int64_t max_seq_q,
+                               int64_t max_seq_kv, int64_t head_dim, const int32_t* cu_seqlens_q,
+                               const int32_t* cu_seqlens_kv, const int64_t q_strides[2], const int64_t k_strides[2],
+                               float sm_scale, unsigned flags, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+                               float* k_scale, float* k_mean, void* workspace, size_t workspace_bytes, void* stream);
+
+int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch, int64_t heads_q,
+                    int64_t heads_kv, int64_t total_q, int64_t total_kv, int64_t max_seq_q, int64_t max_seq_kv,
+                    int64_t head_dim, const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv,
+                    const int64_t q_strides[2], const int64_t k_strides[2], const int64_t v_strides[2],
+                    const int64_t o_strides[2], int causal, float sm_scale, int pv_mode, unsigned flags,
+                    int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean, uint8_t* v_fp8,
+                    float* v_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+int sage_flash_attn_varlen_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,
+                               int64_t heads_q, int64_t heads_kv, int64_t total_q, int64_t total_kv,
+                               int64_t max_seq_q, int64_t max_seq_kv, int64_t head_dim, const int32_t* cu_seqlens_q,
+                               const int32_t* cu_seqlens_kv, const int64_t q_strides[2], const int64_t k_strides[2],
+                               const int64_t v_strides[2], const int64_t o_strides[2], int causal, float sm_scale,
+                               void* stream);
+
+/*
  * Synchronise `stream`, then read and clear the device-side status word of the current
  * device (SAGE_DEV_* bits; 0 = no wait ran out). Returns SAGE_OK, or SAGE_ERR_TIMEOUT
  * when any bit was set, or SAGE_ERR_CUDA.

@@ -81,3 +81,11 @@ def test_gate_chunked_counts_a_planted_error():
     out[0, 1, 17, 3] += 0.5
     r = harness.gate_chunked(out, q, k, v, dtype_str="fp16", atol=5e-2, rtol=5e-2, budget_bytes=1)
     assert not r["passed"] and r["n_fail"] == 1 and r["max_abs_err"] >= 0.49
+
+
+def test_gate_chunked_reports_worst_location():
+    q, k, v = _qkv(2, 3, 3, 50, 50, 16, seed=7, dtype=torch.float16)
+    out = harness.ref_chunked(q, k, v, causal=True)
+    out[1, 2, 33, 9] += 0.25
+    r = harness.gate_chunked(out, q, k, v, True, dtype_str="fp16", atol=5e-2, rtol=5e-2, budget_bytes=600)
+    assert r["worst"] == (1, 2, 33, 9) and r["n_fail"] == 1

@@ -50,6 +50,12 @@ SIGNATURES = {
                       _I, _F, _I, _U, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "sage_flash_attn_fwd": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _I64P,
                                  _I, _F, _P]),
+    "sage_per_block_int8_varlen": (_I, [_P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P,
+                                        _I64P, _I64P, _F, _U, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "sage_run_varlen": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P,
+                             _I64P, _I64P, _I64P, _I64P, _I, _F, _I, _U, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "sage_flash_attn_varlen_fwd": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P,
+                                        _I64P, _I64P, _I64P, _I64P, _I, _F, _P]),
     "sage_device_status": (_I, [ctypes.POINTER(ctypes.c_int), _P]),
     "sage_watchdog_selftest": (_I, [_U, _P]),
 }
@@ -99,3 +105,7 @@ def check(fn: str, rc: int) -> None:
 def strides3(*vals) -> ctypes.Array:
     arr = (ctypes.c_int64 * 3)(*[int(x) for x in vals])
     return arr
+
+
+def strides2(*vals) -> ctypes.Array:
+    return (ctypes.c_int64 * 2)(*[int(x) for x in vals])

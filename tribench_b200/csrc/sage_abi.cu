@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cmath>
@@ -124,6 +125,14 @@ size_t ws_vmax_bytes(int64_t B, int64_t Hkv, int64_t Skv, int64_t D) {
 }
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Variable-length batches: the device prefix sums of sequence lengths and the token rows of the
+// packed tensors. A null Varlen* means dense [B, H, S, D] tensors.
+struct Varlen {
+  const int* cu_q;
+  const int* cu_k;
+  int64_t q_tokens, k_tokens;
+};
+
 int encode_4d(CUtensorMap* map, CUtensorMapDataType dt, int elt_bytes, const void* base, int64_t d0, int64_t d1,
               int64_t d2, int64_t d3, int64_t s1, int64_t s2, int64_t s3, uint32_t box0, uint32_t box1,
               CUtensorMapSwizzle sw) {
@@ -152,7 +161,7 @@ template <int D, typename T>
 int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                    int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs, float q_mult, bool smooth,
                    bool km_given, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean,
-                   uint8_t* v_fp8, float* v_scale, void* ws, cudaStream_t st) {
+                   uint8_t* v_fp8, float* v_scale, void* ws, const Varlen* vl, cudaStream_t st) {
   const int nchunk = static_cast<int>(cdiv(Skv, sage::kStatsChunk));
   const bool want_v = v_fp8 != nullptr;
   const bool want_km = smooth && !km_given && k != nullptr;
@@ -166,6 +175,7 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
   p.v_fp8 = v_fp8; p.v_scale = v_scale;
   p.q_mult = q_mult;
   p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
+  if (vl) { p.cu_q = vl->cu_q; p.cu_k = vl->cu_k; p.q_tokens = (int)vl->q_tokens; p.k_tokens = (int)vl->k_tokens; }
   p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, sage::kVRowsPerCta<D>); p.nchunk = nchunk;
   const int64_t n_q = q ? B * Hq * cdiv(p.nqb, sage::kQBlocksPerCta<D>) : 0;
   const int64_t n_k = k ? B * Hkv * cdiv(p.nkb, sage::kKBlocksPerCta<D>) : 0;
@@ -187,13 +197,15 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
   p.n_v = 0;
   const int64_t grid_a = (int64_t)p.n_q + p.n_stat + p.n_k;
   if (grid_a > 0) {
-    sage::prepass_kernel<D, T><<<(unsigned)grid_a, sage::kQuantThreads, 0, st>>>(p);
+    if (vl) sage::prepass_kernel<D, T, true><<<(unsigned)grid_a, sage::kQuantThreads, 0, st>>>(p);
+    else sage::prepass_kernel<D, T, false><<<(unsigned)grid_a, sage::kQuantThreads, 0, st>>>(p);
     SAGE_CUDA_TRY(cudaGetLastError());
   }
   if (need_stats) {
     sage::FinalizeParams fp{};
     fp.ksum_part = p.ksum_part; fp.vmax_part = p.vmax_part; fp.k_mean = k_mean; fp.v_scale = v_scale;
     fp.Hkv = (int)Hkv; fp.S = (int)Skv; fp.nchunk = nchunk; fp.D = D;
+    if (vl) { fp.cu = vl->cu_k; fp.tokens = (int)vl->k_tokens; }
     sage::kv_finalize_kernel<<<dim3((unsigned)Hkv, (unsigned)B), 128, 0, st>>>(fp);
     SAGE_CUDA_TRY(cudaGetLastError());
     // launch B: K blocks that needed the mean, and V blocks
@@ -203,7 +215,8 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
     p.n_v = (int)n_v;
     const int64_t grid_b = (int64_t)p.n_k + p.n_v;
     if (grid_b > 0) {
-      sage::prepass_kernel<D, T><<<(unsigned)grid_b, sage::kQuantThreads, 0, st>>>(p);
+      if (vl) sage::prepass_kernel<D, T, true><<<(unsigned)grid_b, sage::kQuantThreads, 0, st>>>(p);
+      else sage::prepass_kernel<D, T, false><<<(unsigned)grid_b, sage::kQuantThreads, 0, st>>>(p);
       SAGE_CUDA_TRY(cudaGetLastError());
     }
   }
@@ -213,19 +226,20 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
 int prepass_dispatch(int dtype, int64_t D, const void* q, const void* k, const void* v, int64_t B, int64_t Hq,
                      int64_t Hkv, int64_t Sq, int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                      float q_mult, bool smooth, bool km_given, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale,
-                     float* k_mean, uint8_t* v_fp8, float* v_scale, void* ws, cudaStream_t st) {
+                     float* k_mean, uint8_t* v_fp8, float* v_scale, void* ws, cudaStream_t st,
+                     const Varlen* vl = nullptr) {
   if (dtype == SAGE_DTYPE_F16) {
     if (D == 128)
       return launch_prepass<128, __half>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale, k_i8,
-                                         k_scale, k_mean, v_fp8, v_scale, ws, st);
+                                         k_scale, k_mean, v_fp8, v_scale, ws, vl, st);
     return launch_prepass<64, __half>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale, k_i8,
-                                      k_scale, k_mean, v_fp8, v_scale, ws, st);
+                                      k_scale, k_mean, v_fp8, v_scale, ws, vl, st);
   }
   if (D == 128)
     return launch_prepass<128, __nv_bfloat16>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale,
-                                              k_i8, k_scale, k_mean, v_fp8, v_scale, ws, st);
+                                              k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, st);
   return launch_prepass<64, __nv_bfloat16>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale,
-                                           k_i8, k_scale, k_mean, v_fp8, v_scale, ws, st);
+                                           k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, st);
 }
 
 // ---------------------------------------------------------------- attention launch
@@ -242,37 +256,53 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
   return SAGE_OK;
 }
 
-int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale, const void* v,
-              const int64_t* vs, const float* v_scale, void* o, const int64_t* os, int dtype, int pv_mode, int causal,
-              int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, cudaStream_t st) {
-  const bool fp8 = pv_mode == SAGE_PV_FP8;
-  CUtensorMap tq, tk, tv;
-  const CUtensorMapSwizzle swqk = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  if (int rc = encode_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q_i8, D, Sq, Hq, B, D, Sq * D, Hq * Sq * D,
-                         (uint32_t)D, 128, swqk))
-    return rc;
-  if (int rc = encode_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k_i8, D, Skv, Hkv, B, D, Skv * D, Hkv * Skv * D,
-                         (uint32_t)D, 128, swqk))
-    return rc;
-  if (fp8) {
-    if (int rc = encode_4d(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, v, D, Skv, Hkv, B, D, Skv * D, Hkv * Skv * D,
-                           (uint32_t)D, 128, swqk))
-      return rc;
-  } else {
-    const CUtensorMapDataType dt =
-        dtype == SAGE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if (int rc = encode_4d(&tv, dt, 2, v, D, Skv, Hkv, B, vs[2], vs[1], vs[0], 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
-      return rc;
-  }
-  sage::AttnParams p{};
-  p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.o = o;
-  p.o_sb = os[0]; p.o_sh = os[1]; p.o_ss = os[2];
+// Batch stride (elements) for a tensor map over packed sequences, whose batch extent is 1: any
+// valid stride serves; this one covers the whole tensor.
+int64_t packed_batch_stride(const int64_t* s, int64_t H, int64_t rows) { return std::max(s[1] * H, s[2] * rows); }
+
+// Sets the tensor-shape fields that dense and packed batches share; rows / batch extents of the
+// tensor maps come from here too.
+void set_seq_params(sage::AttnParams& p, const Varlen* vl, const int64_t* os, int64_t B, int64_t Hq, int64_t Hkv,
+                    int64_t Sq, int64_t Skv, int causal) {
+  p.o_sb = vl ? 0 : os[0]; p.o_sh = os[1]; p.o_ss = os[2];
   p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
   p.groups = (int)(Hq / Hkv);
   p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64);
   p.causal = causal ? 1 : 0;
   p.n_m_ctas = (int)cdiv(Sq, 256);
   p.wait_limit_ns = wait_limit_ns();
+  if (vl) { p.cu_q = vl->cu_q; p.cu_k = vl->cu_k; p.q_tokens = (int)vl->q_tokens; p.k_tokens = (int)vl->k_tokens; }
+}
+
+int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale, const void* v,
+              const int64_t* vs, const float* v_scale, void* o, const int64_t* os, int dtype, int pv_mode, int causal,
+              int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, cudaStream_t st,
+              const Varlen* vl = nullptr) {
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  // rows of the token axis and batch extent of every tensor map (packed sequences: one batch)
+  const int64_t rq = vl ? vl->q_tokens : Sq, rk = vl ? vl->k_tokens : Skv, nb = vl ? 1 : B;
+  CUtensorMap tq, tk, tv;
+  const CUtensorMapSwizzle swqk = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (int rc = encode_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q_i8, D, rq, Hq, nb, D, rq * D, Hq * rq * D,
+                         (uint32_t)D, 128, swqk))
+    return rc;
+  if (int rc = encode_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k_i8, D, rk, Hkv, nb, D, rk * D, Hkv * rk * D,
+                         (uint32_t)D, 128, swqk))
+    return rc;
+  if (fp8) {
+    if (int rc = encode_4d(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, v, D, rk, Hkv, nb, D, rk * D, Hkv * rk * D,
+                           (uint32_t)D, 128, swqk))
+      return rc;
+  } else {
+    const CUtensorMapDataType dt =
+        dtype == SAGE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (int rc = encode_4d(&tv, dt, 2, v, D, rk, Hkv, nb, vs[2], vs[1], vl ? packed_batch_stride(vs, Hkv, rk) : vs[0],
+                           64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  sage::AttnParams p{};
+  p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.o = o;
+  set_seq_params(p, vl, os, B, Hq, Hkv, Sq, Skv, causal);
   const bool obf = dtype == SAGE_DTYPE_BF16;
   if (D == 128) {
     if (fp8) return obf ? launch_attn<128, sage::kPvE4M3, true>(tq, tk, tv, p, st)
@@ -289,25 +319,23 @@ int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, cons
 // flash_attn pack: the same pipeline on fp16/bf16 Q and K (no pre-pass)
 int flash_impl(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v, const int64_t* vs,
                void* o, const int64_t* os, int dtype, int causal, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
-               int64_t Skv, int64_t D, float sm_scale, cudaStream_t st) {
+               int64_t Skv, int64_t D, float sm_scale, cudaStream_t st, const Varlen* vl = nullptr) {
   const CUtensorMapDataType dt =
       dtype == SAGE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t rq = vl ? vl->q_tokens : Sq, rk = vl ? vl->k_tokens : Skv, nb = vl ? 1 : B;
   CUtensorMap tq, tk, tv;
-  if (int rc = encode_4d(&tq, dt, 2, q, D, Sq, Hq, B, qs[2], qs[1], qs[0], 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (int rc = encode_4d(&tq, dt, 2, q, D, rq, Hq, nb, qs[2], qs[1], vl ? packed_batch_stride(qs, Hq, rq) : qs[0], 64,
+                         128, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if (int rc = encode_4d(&tk, dt, 2, k, D, Skv, Hkv, B, ks[2], ks[1], ks[0], 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (int rc = encode_4d(&tk, dt, 2, k, D, rk, Hkv, nb, ks[2], ks[1], vl ? packed_batch_stride(ks, Hkv, rk) : ks[0],
+                         64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if (int rc = encode_4d(&tv, dt, 2, v, D, Skv, Hkv, B, vs[2], vs[1], vs[0], 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (int rc = encode_4d(&tv, dt, 2, v, D, rk, Hkv, nb, vs[2], vs[1], vl ? packed_batch_stride(vs, Hkv, rk) : vs[0],
+                         64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   sage::AttnParams p{};
   p.o = o;
-  p.o_sb = os[0]; p.o_sh = os[1]; p.o_ss = os[2];
-  p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
-  p.groups = (int)(Hq / Hkv);
-  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64);
-  p.causal = causal ? 1 : 0;
-  p.n_m_ctas = (int)cdiv(Sq, 256);
-  p.wait_limit_ns = wait_limit_ns();
+  set_seq_params(p, vl, os, B, Hq, Hkv, Sq, Skv, causal);
   const double s = sm_scale > 0.0f ? static_cast<double>(sm_scale) : 1.0 / std::sqrt(static_cast<double>(D));
   p.qk_scale = static_cast<float>(s * 1.4426950408889634);  // exp(x) = exp2(x * log2(e))
   if (dtype == SAGE_DTYPE_BF16)
@@ -581,6 +609,132 @@ int sage_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, in
   if (int rc = check_arch()) return rc;
   return flash_impl(q, q_strides, k, k_strides, v, v_strides, o, o_strides, dtype, causal, batch, heads_q, heads_kv,
                     seq_q, seq_kv, head_dim, sm_scale, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+// Shared validation of the variable-length entry points. The cu arrays live on the device and
+// are not read here: the kernels clamp every sequence to [0, max_seq] rows inside the tokens.
+int check_varlen(int dtype, int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t total_q, int64_t total_kv,
+                 int64_t max_seq_q, int64_t max_seq_kv, int64_t head_dim, const int32_t* cu_q, const int32_t* cu_kv) {
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, max_seq_q, max_seq_kv, head_dim)) return rc;
+  if (total_q <= 0 || total_kv <= 0 || total_q > 0x7fffffffLL || total_kv > 0x7fffffffLL)
+    return fail(SAGE_ERR_INVALID_ARG, "total_q=%lld / total_kv=%lld outside [1, 2^31)", (long long)total_q,
+                (long long)total_kv);
+  if (max_seq_q > total_q || max_seq_kv > total_kv)
+    return fail(SAGE_ERR_INVALID_ARG, "max_seq_q=%lld / max_seq_kv=%lld exceed the token counts %lld / %lld",
+                (long long)max_seq_q, (long long)max_seq_kv, (long long)total_q, (long long)total_kv);
+  if (!cu_q || !cu_kv || (reinterpret_cast<uintptr_t>(cu_q) & 3u) || (reinterpret_cast<uintptr_t>(cu_kv) & 3u))
+    return fail(SAGE_ERR_INVALID_ARG, "cu_seqlens_q / cu_seqlens_kv must be 4-byte aligned device pointers");
+  return SAGE_OK;
+}
+
+// {head, token} strides of a packed tensor -> the {batch, head, seq} form used inside (batch 0).
+int packed_strides(const char* name, const int64_t* s2, int64_t out[3]) {
+  if (!s2) return fail(SAGE_ERR_INVALID_ARG, "%s strides are NULL", name);
+  for (int i = 0; i < 2; ++i)
+    if (s2[i] <= 0 || (s2[i] % 8) != 0)
+      return fail(SAGE_ERR_INVALID_ARG, "%s stride[%d]=%lld must be a positive multiple of 8 elements", name, i,
+                  (long long)s2[i]);
+  out[0] = 0; out[1] = s2[0]; out[2] = s2[1];
+  return SAGE_OK;
+}
+}  // namespace
+
+int sage_per_block_int8_varlen(const void* q, const void* k, int dtype, int64_t batch, int64_t heads_q,
+                               int64_t heads_kv, int64_t total_q, int64_t total_kv, int64_t max_seq_q,
+                               int64_t max_seq_kv, int64_t head_dim, const int32_t* cu_seqlens_q,
+                               const int32_t* cu_seqlens_kv, const int64_t q_strides[2], const int64_t k_strides[2],
+                               float sm_scale, unsigned flags, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+                               float* k_scale, float* k_mean, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_varlen(dtype, batch, heads_q, heads_kv, total_q, total_kv, max_seq_q, max_seq_kv, head_dim,
+                            cu_seqlens_q, cu_seqlens_kv))
+    return rc;
+  int64_t qs[3], ks[3];
+  if (int rc = packed_strides("q", q_strides, qs)) return rc;
+  if (int rc = packed_strides("k", k_strides, ks)) return rc;
+  if (!q || !k || !q_i8 || !q_scale || !k_i8 || !k_scale) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(q_i8) || !aligned16(k_i8))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k/q_i8/k_i8 must be 16-byte aligned");
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
+  const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
+  const size_t need = km_given ? 0 : sage_workspace_bytes(batch, heads_kv, max_seq_kv, head_dim, SAGE_PV_16BIT, flags);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (int rc = check_arch()) return rc;
+  const Varlen vl{cu_seqlens_q, cu_seqlens_kv, total_q, total_kv};
+  return prepass_dispatch(dtype, head_dim, q, k, nullptr, batch, heads_q, heads_kv, max_seq_q, max_seq_kv, qs, ks,
+                          nullptr, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8, q_scale, k_i8, k_scale,
+                          k_mean, nullptr, nullptr, workspace, static_cast<cudaStream_t>(stream), &vl);
+}
+
+int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch, int64_t heads_q,
+                    int64_t heads_kv, int64_t total_q, int64_t total_kv, int64_t max_seq_q, int64_t max_seq_kv,
+                    int64_t head_dim, const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv,
+                    const int64_t q_strides[2], const int64_t k_strides[2], const int64_t v_strides[2],
+                    const int64_t o_strides[2], int causal, float sm_scale, int pv_mode, unsigned flags,
+                    int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean, uint8_t* v_fp8,
+                    float* v_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_varlen(dtype, batch, heads_q, heads_kv, total_q, total_kv, max_seq_q, max_seq_kv, head_dim,
+                            cu_seqlens_q, cu_seqlens_kv))
+    return rc;
+  int64_t qs[3], ks[3], vs[3], os[3];
+  if (int rc = packed_strides("q", q_strides, qs)) return rc;
+  if (int rc = packed_strides("k", k_strides, ks)) return rc;
+  if (int rc = packed_strides("v", v_strides, vs)) return rc;
+  if (int rc = packed_strides("o", o_strides, os)) return rc;
+  if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
+    return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
+  if (!q || !k || !v || !o || !q_i8 || !q_scale || !k_i8 || !k_scale)
+    return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(q_i8) || !aligned16(k_i8))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o/q_i8/k_i8 must be 16-byte aligned");
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
+  if (fp8 && (!v_fp8 || !v_scale || !aligned16(v_fp8)))
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs 16-byte aligned v_fp8 and v_scale");
+  const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
+  const size_t need = sage_workspace_bytes(batch, heads_kv, max_seq_kv, head_dim, pv_mode, km_given ? 0u : flags);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (int rc = check_arch()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Varlen vl{cu_seqlens_q, cu_seqlens_kv, total_q, total_kv};
+  if (int rc = prepass_dispatch(dtype, head_dim, q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv, max_seq_q,
+                                max_seq_kv, qs, ks, vs, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8,
+                                q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr,
+                                workspace, st, &vl))
+    return rc;
+  return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, vs,
+                   fp8 ? v_scale : nullptr, o, os, dtype, pv_mode, causal, batch, heads_q, heads_kv, max_seq_q,
+                   max_seq_kv, head_dim, st, &vl);
+}
+
+int sage_flash_attn_varlen_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,
+                               int64_t heads_q, int64_t heads_kv, int64_t total_q, int64_t total_kv,
+                               int64_t max_seq_q, int64_t max_seq_kv, int64_t head_dim, const int32_t* cu_seqlens_q,
+                               const int32_t* cu_seqlens_kv, const int64_t q_strides[2], const int64_t k_strides[2],
+                               const int64_t v_strides[2], const int64_t o_strides[2], int causal, float sm_scale,
+                               void* stream) {
+  g_last_error.clear();
+  if (int rc = check_varlen(dtype, batch, heads_q, heads_kv, total_q, total_kv, max_seq_q, max_seq_kv, head_dim,
+                            cu_seqlens_q, cu_seqlens_kv))
+    return rc;
+  int64_t qs[3], ks[3], vs[3], os[3];
+  if (int rc = packed_strides("q", q_strides, qs)) return rc;
+  if (int rc = packed_strides("k", k_strides, ks)) return rc;
+  if (int rc = packed_strides("v", v_strides, vs)) return rc;
+  if (int rc = packed_strides("o", o_strides, os)) return rc;
+  if (!q || !k || !v || !o) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o must be 16-byte aligned");
+  if (int rc = check_arch()) return rc;
+  const Varlen vl{cu_seqlens_q, cu_seqlens_kv, total_q, total_kv};
+  return flash_impl(q, qs, k, ks, v, vs, o, os, dtype, causal, batch, heads_q, heads_kv, max_seq_q, max_seq_kv,
+                    head_dim, sm_scale, static_cast<cudaStream_t>(stream), &vl);
 }
 
 int sage_device_status(int* status_bits, void* stream) {

@@ -30,6 +30,7 @@
 //     PV_t(j-1) to finish (pvdone) before it writes P_t(j) or rescales O_t.
 #pragma once
 
+#include "sage_seq.cuh"
 #include "sm100_ptx.cuh"
 
 namespace sage {
@@ -42,8 +43,14 @@ struct AttnParams {
   const float* v_scale;  // [B, Hkv, D]  (e4m3 P.V only)
   void* o;
   int64_t o_sb, o_sh, o_ss;  // output strides, elements
-  int B, Hq, Hkv, Sq, Skv, groups;
+  int B, Hq, Hkv, Sq, Skv, groups;  // variable-length batches: Sq / Skv = longest sequence
   int nqb, nkb;
+  // Variable-length batches (nullable): sequence b owns token rows [cu_q[b], cu_q[b+1]) of Q/O
+  // and [cu_k[b], cu_k[b+1]) of K/V, whose tensors have batch extent 1 and q_tokens / k_tokens
+  // rows; the scales stay [B, H, nqb / nkb] per sequence.
+  const int* cu_q;
+  const int* cu_k;
+  int q_tokens, k_tokens;
   int causal;
   int n_m_ctas;              // CTAs along the query axis
   unsigned long long wait_limit_ns;
@@ -188,7 +195,11 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int hkv = h / p.groups;
-  const int nkv_all = (p.Skv + C::BN - 1) / C::BN;
+  const SeqSpan sq = seq_span(p.cu_q, b, p.Sq, p.q_tokens);
+  const SeqSpan sk = seq_span(p.cu_k, b, p.Skv, p.k_tokens);
+  const int Sq = sq.len, Skv = sk.len;
+  const int nkb_seq = (Skv + 63) / 64;  // 64-key scale blocks of this sequence
+  const int nkv_all = (Skv + C::BN - 1) / C::BN;
 
   // Key tiles each query tile needs (0 for a tile entirely past seq_q).
   int nkv[QT];
@@ -198,7 +209,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
     const int r0 = (m_cta * QT + t) * C::BM;
     int n = nkv_all;
     if (p.causal) n = min(n, r0 / C::BN + 1);
-    if (r0 >= p.Sq) n = 0;
+    if (r0 >= Sq) n = 0;
     nkv[t] = n;
     nkv_max = max(nkv_max, n);
   }
@@ -255,7 +266,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
 #pragma unroll
         for (int x = 0; x < C::QK_ATOMS; ++x)
           tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE + x * (C::BM * 128), &tmQ, bar_q, x * C::QK_BOX,
-                      (m_cta * QT + t) * C::BM, h, b);
+                      sq.base + (m_cta * QT + t) * C::BM, h, sq.batch);
       for (int j = 0; j < nkv_max; ++j) {
         const int s = j % C::NS;
         SAGE_T_MARK(1)
@@ -267,12 +278,12 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
 #pragma unroll
         for (int x = 0; x < C::QK_ATOMS; ++x)
           tma_load_4d(smem + C::OFF_K + s * C::K_TILE + x * (C::BN * 128), &tmK, bar_kfull + s, x * C::QK_BOX,
-                      j * C::BN, hkv, b);
+                      sk.base + j * C::BN, hkv, sk.batch);
         mbar_arrive_expect_tx(bar_vfull + s, C::V_TILE);
 #pragma unroll
         for (int x = 0; x < C::V_BOXES; ++x)
           tma_load_4d(smem + C::OFF_V + s * C::V_TILE + x * (C::BN * 128), &tmV, bar_vfull + s,
-                      x * (128 / C::V_ELT), j * C::BN, hkv, b);
+                      x * (128 / C::V_ELT), sk.base + j * C::BN, hkv, sk.batch);
       }
     }
     SAGE_T_FLUSH(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), warp)
@@ -418,8 +429,8 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
       }
       SAGE_T_MARK(1)
       const int key0 = j * C::BN;
-      if ((key0 + C::BN > p.Skv) || (p.causal && key0 + C::BN - 1 > r0)) {
-        const int lim = (p.causal ? min(p.Skv, row + 1) : p.Skv) - key0;  // visible keys: [0, lim)
+      if ((key0 + C::BN > Skv) || (p.causal && key0 + C::BN - 1 > r0)) {
+        const int lim = (p.causal ? min(Skv, row + 1) : Skv) - key0;  // visible keys: [0, lim)
 #pragma unroll
         for (int c = 0; c < 128; ++c)
           if (c >= lim) b[c] = -INFINITY;
@@ -440,7 +451,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
       // a zero scale (all-zero block) is replaced by FLT_MIN: its scores are exactly 0 either
       // way, and masked -inf entries stay -inf instead of becoming NaN
       const float sc0 = FLASH ? p.qk_scale : fmaxf(qs * ksp[kb0], 1.17549435e-38f);
-      const float sc1 = FLASH ? p.qk_scale : ((kb0 + 1 < p.nkb) ? fmaxf(qs * ksp[kb0 + 1], 1.17549435e-38f) : sc0);
+      const float sc1 = FLASH ? p.qk_scale : ((kb0 + 1 < nkb_seq) ? fmaxf(qs * ksp[kb0 + 1], 1.17549435e-38f) : sc0);
       const float tmax = fmaxf((hm[0] - kMagic) * sc0, (hm[1] - kMagic) * sc1);
       const bool upd = tmax > m_run + C::LAZY;
       const float m_new = upd ? tmax : m_run;
@@ -522,13 +533,13 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
     }
     SAGE_T_MARK(5)
     // ---------------------------------------------------------- epilogue
+    const bool valid = row < Sq;
+    char* orow_ptr = reinterpret_cast<char*>(p.o) +
+                     ((int64_t)sq.batch * p.o_sb + (int64_t)h * p.o_sh + (int64_t)(sq.base + row) * p.o_ss) * 2;
     if (ok && n > 0 &&
         __all_sync(0xffffffffu, mbar_wait(bar_odone + t, 0, abort_flag, kDevTimeoutEpilogue, p.wait_limit_ns))) {
       tc_fence_after();
       const float inv_l = 1.0f / l_run;
-      const bool valid = row < p.Sq;
-      char* orow_ptr = reinterpret_cast<char*>(p.o) +
-                       ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_ss) * 2;
       const float* vsp = p.v_scale + ((size_t)b * p.Hkv + hkv) * D;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 32) {
@@ -558,6 +569,12 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
             dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
         }
       }
+    } else if (Skv == 0 && valid) {
+      // a sequence without keys (variable-length batches): the reference's matmuls over an
+      // empty key axis give O = 0
+      uint4* dst = reinterpret_cast<uint4*>(orow_ptr);
+#pragma unroll
+      for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(0u, 0u, 0u, 0u);
     }
     SAGE_T_MARK(6)
     SAGE_T_FLUSH(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), warp)

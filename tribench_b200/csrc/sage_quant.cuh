@@ -24,6 +24,7 @@
 //   B: K quantisation (smoothed) + V to e4m3
 #pragma once
 
+#include "sage_seq.cuh"
 #include "sm100_ptx.cuh"
 
 namespace sage {
@@ -149,8 +150,14 @@ struct PrepassParams {
   double* ksum_part;    // statistics: [B, Hkv, nchunk, D]
   float* vmax_part;     // statistics: [B, Hkv, nchunk, D]
   float q_mult;
-  int B, Hq, Hkv, Sq, Skv;
+  int B, Hq, Hkv, Sq, Skv;  // variable-length batches: Sq / Skv = longest sequence
   int nqb, nkb, nvb, nchunk;
+  // Variable-length batches (nullable): sequence b owns token rows [cu_q[b], cu_q[b+1]) of Q and
+  // [cu_k[b], cu_k[b+1]) of K/V (batch extent 1, q_tokens / k_tokens rows); the int8 / e4m3
+  // outputs are [H, tokens, D], the scales and statistics stay per sequence.
+  const int* cu_q;
+  const int* cu_k;
+  int q_tokens, k_tokens;
   // CTA roles of this launch, in grid order: Q blocks, statistics chunks, K blocks, V blocks
   int n_q, n_stat, n_k, n_v;
   int stat_k, stat_v;   // which statistics the statistics CTAs gather
@@ -158,7 +165,7 @@ struct PrepassParams {
 
 // ---------------------------------------------------------------- roles
 // NSUB consecutive scale blocks of BLK rows, all rows loaded up front.
-template <int D, typename T, int BLK, int NSUB>
+template <int D, typename T, int BLK, int NSUB, bool PACKED>
 __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta, bool isq, float* red) {
   constexpr int TPR = D / 8;                 // threads per row (8 channels each)
   constexpr int RPP = kQuantThreads / TPR;   // rows per pass
@@ -168,14 +175,19 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
   const int nb = isq ? p.nqb : p.nkb;
   const int ng = (nb + NSUB - 1) / NSUB;     // CTAs per head
   const int H = isq ? p.Hq : p.Hkv;
-  const int S = isq ? p.Sq : p.Skv;
   const int grp = cta % ng;
   const int hh = (cta / ng) % H;
   const int bb = cta / (ng * H);
-  const char* src = reinterpret_cast<const char*>(isq ? p.q : p.k) +
-                    (bb * (isq ? p.q_sb : p.k_sb) + hh * (isq ? p.q_sh : p.k_sh)) * (int64_t)sizeof(T) + g * 16;
-  const int64_t ss = (isq ? p.q_ss : p.k_ss) * (int64_t)sizeof(T);
+  const SeqSpan sp = isq ? seq_span(PACKED ? p.cu_q : nullptr, bb, p.Sq, p.q_tokens)
+                          : seq_span(PACKED ? p.cu_k : nullptr, bb, p.Skv, p.k_tokens);
+  const int S = sp.len;
   const int row0 = grp * NSUB * BLK;
+  if (row0 >= S) return;  // a block past the end of a shorter sequence (uniform over the CTA)
+  const int64_t ss_elts = isq ? p.q_ss : p.k_ss;
+  const char* src = reinterpret_cast<const char*>(isq ? p.q : p.k) +
+                    (sp.batch * (isq ? p.q_sb : p.k_sb) + hh * (isq ? p.q_sh : p.k_sh) + sp.base * ss_elts) *
+                        (int64_t)sizeof(T) + g * 16;
+  const int64_t ss = ss_elts * (int64_t)sizeof(T);
   const bool smooth = !isq && p.k_mean != nullptr;
   float km[8];
 #pragma unroll
@@ -227,7 +239,8 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
 #pragma unroll
   for (int b = 0; b < NSUB; ++b)
     if (threadIdx.x == b && grp * NSUB + b < nb) (isq ? p.q_scale : p.k_scale)[head * nb + grp * NSUB + b] = scale[b];
-  int8_t* dst = (isq ? p.q_i8 : p.k_i8) + head * (size_t)S * D + g * 8;
+  const size_t first_row = PACKED ? (size_t)hh * (isq ? p.q_tokens : p.k_tokens) + sp.base : head * (size_t)S;
+  int8_t* dst = (isq ? p.q_i8 : p.k_i8) + first_row * D + g * 8;
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const int row = row0 + r + i * RPP;
@@ -251,7 +264,7 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
 }
 
 // Statistics over one chunk of kStatsChunk rows: fp64 column sums of K, fp32 column absmax of V.
-template <int D, typename T>
+template <int D, typename T, bool PACKED>
 __device__ __forceinline__ void stats_role(const PrepassParams& p, int cta, double (*sum_red)[D], float (*max_red)[D]) {
   constexpr int TPR = D / 8;
   constexpr int RPP = kQuantThreads / TPR;
@@ -260,15 +273,18 @@ __device__ __forceinline__ void stats_role(const PrepassParams& p, int cta, doub
   const int h = (cta / p.nchunk) % p.Hkv;
   const int b = cta / (p.nchunk * p.Hkv);
   const int g = threadIdx.x % TPR, r = threadIdx.x / TPR;
+  const SeqSpan sp = seq_span(PACKED ? p.cu_k : nullptr, b, p.Skv, p.k_tokens);
   const int row0 = c * kStatsChunk;
-  const int row1 = min(p.Skv, row0 + kStatsChunk);
+  const int row1 = min(sp.len, row0 + kStatsChunk);  // chunks past the end contribute zeros
   double acc[8];
   float amax[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) { acc[i] = 0.0; amax[i] = 0.0f; }
-  const char* kb = p.stat_k ? reinterpret_cast<const char*>(p.k) + (b * p.k_sb + h * p.k_sh) * (int64_t)sizeof(T) + g * 16
+  const char* kb = p.stat_k ? reinterpret_cast<const char*>(p.k) +
+                                  (sp.batch * p.k_sb + h * p.k_sh + sp.base * p.k_ss) * (int64_t)sizeof(T) + g * 16
                             : nullptr;
-  const char* vb = p.stat_v ? reinterpret_cast<const char*>(p.v) + (b * p.v_sb + h * p.v_sh) * (int64_t)sizeof(T) + g * 16
+  const char* vb = p.stat_v ? reinterpret_cast<const char*>(p.v) +
+                                  (sp.batch * p.v_sb + h * p.v_sh + sp.base * p.v_ss) * (int64_t)sizeof(T) + g * 16
                             : nullptr;
   for (int base = row0 + r; base < row1; base += U * RPP) {
     uint4 kr[U], vr[U];
@@ -321,7 +337,7 @@ __device__ __forceinline__ void stats_role(const PrepassParams& p, int cta, doub
 
 // V -> e4m3 with per-channel scales, kVRowsPerCta rows per CTA: v / v_scale (correctly rounded quotient),
 // then cvt.rn.satfinite; a channel whose scale is 0 gives 0.
-template <int D, typename T>
+template <int D, typename T, bool PACKED>
 __device__ __forceinline__ void vquant_role(const PrepassParams& p, int cta) {
   constexpr int TPR = D / 8;
   constexpr int RPP = kQuantThreads / TPR;
@@ -330,25 +346,30 @@ __device__ __forceinline__ void vquant_role(const PrepassParams& p, int cta) {
   const int hh = (cta / p.nvb) % p.Hkv;
   const int bb = cta / (p.nvb * p.Hkv);
   const size_t head = (size_t)bb * p.Hkv + hh;
-  const char* src = reinterpret_cast<const char*>(p.v) + (bb * p.v_sb + hh * p.v_sh) * (int64_t)sizeof(T) + g * 16;
+  const SeqSpan sp = seq_span(PACKED ? p.cu_k : nullptr, bb, p.Skv, p.k_tokens);
+  const int S = sp.len;
+  if (blk * kVRowsPerCta<D> >= S) return;  // past the end of a shorter sequence (uniform)
+  const char* src = reinterpret_cast<const char*>(p.v) +
+                    (sp.batch * p.v_sb + hh * p.v_sh + sp.base * p.v_ss) * (int64_t)sizeof(T) + g * 16;
   float vs[8], rv[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     vs[e] = p.v_scale[head * D + g * 8 + e];
     rv[e] = __frcp_rn(vs[e]);
   }
-  uint8_t* dst = p.v_fp8 + head * (size_t)p.Skv * D + g * 8;
+  const size_t first_row = PACKED ? (size_t)hh * p.k_tokens + sp.base : head * (size_t)S;
+  uint8_t* dst = p.v_fp8 + first_row * D + g * 8;
   constexpr int NP = kVRowsPerCta<D> / RPP;
   uint4 raw[NP];
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const int row = blk * kVRowsPerCta<D> + r + i * RPP;
-    raw[i] = (row < p.Skv) ? ldg_nc_v4(src + row * p.v_ss * (int64_t)sizeof(T)) : make_uint4(0u, 0u, 0u, 0u);
+    raw[i] = (row < S) ? ldg_nc_v4(src + row * p.v_ss * (int64_t)sizeof(T)) : make_uint4(0u, 0u, 0u, 0u);
   }
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const int row = blk * kVRowsPerCta<D> + r + i * RPP;
-    if (row >= p.Skv) continue;
+    if (row >= S) continue;
     float f[8];
     Half8<T>::to_float(raw[i], f);
     uint32_t w[2] = {0u, 0u};
@@ -364,22 +385,24 @@ __device__ __forceinline__ void vquant_role(const PrepassParams& p, int cta) {
 }
 
 // One launch of the pre-pass: CTA roles in grid order Q blocks | statistics chunks | K blocks | V blocks.
-template <int D, typename T>
+// PACKED: variable-length batches (p.cu_q / p.cu_k set); a separate instantiation keeps the
+// dense path's code and registers as they are without the sequence offsets.
+template <int D, typename T, bool PACKED>
 __global__ void __launch_bounds__(kQuantThreads) prepass_kernel(PrepassParams p) {
   constexpr int RPP = kQuantThreads / (D / 8);
   __shared__ double sum_red[RPP][D];
   __shared__ float max_red[RPP][D];
   __shared__ float red[4 * (kQuantThreads / 32)];
   int cta = blockIdx.x;
-  if (cta < p.n_q) { quant_block_role<D, T, 128, kQBlocksPerCta<D>>(p, cta, true, red); return; }
+  if (cta < p.n_q) { quant_block_role<D, T, 128, kQBlocksPerCta<D>, PACKED>(p, cta, true, red); return; }
   cta -= p.n_q;
-  if (cta < p.n_stat) { stats_role<D, T>(p, cta, sum_red, max_red); return; }
+  if (cta < p.n_stat) { stats_role<D, T, PACKED>(p, cta, sum_red, max_red); return; }
   cta -= p.n_stat;
   // K and V blocks run in reverse head order: the statistics CTAs of the previous launch read
   // the last heads most recently, so their rows are the ones still in L2
-  if (cta < p.n_k) { quant_block_role<D, T, 64, kKBlocksPerCta<D>>(p, p.n_k - 1 - cta, false, red); return; }
+  if (cta < p.n_k) { quant_block_role<D, T, 64, kKBlocksPerCta<D>, PACKED>(p, p.n_k - 1 - cta, false, red); return; }
   cta -= p.n_k;
-  vquant_role<D, T>(p, p.n_v - 1 - cta);
+  vquant_role<D, T, PACKED>(p, p.n_v - 1 - cta);
 }
 
 struct FinalizeParams {
@@ -388,6 +411,8 @@ struct FinalizeParams {
   float* k_mean;            // [B, Hkv, D]
   float* v_scale;           // [B, Hkv, D]
   int Hkv, S, nchunk, D;
+  const int* cu;            // variable-length batches: K/V sequence b is rows [cu[b], cu[b+1])
+  int tokens;
 };
 
 // Grid (Hkv, B), D threads: km = fp32(sum / S), v_scale = absmax / 448.
@@ -398,7 +423,9 @@ __global__ void kv_finalize_kernel(FinalizeParams p) {
   if (p.ksum_part) {
     double s = 0.0;
     for (int c = 0; c < p.nchunk; ++c) s = __dadd_rn(s, p.ksum_part[(head * p.nchunk + c) * p.D + d]);
-    p.k_mean[head * p.D + d] = __double2float_rn(__ddiv_rn(s, static_cast<double>(p.S)));
+    const int len = seq_span(p.cu, b, p.S, p.tokens).len;
+    // an empty sequence has no K rows to smooth: its mean is never used; 0 keeps it finite
+    p.k_mean[head * p.D + d] = len > 0 ? __double2float_rn(__ddiv_rn(s, static_cast<double>(len))) : 0.0f;
   }
   if (p.vmax_part) {
     float m = 0.0f;

@@ -103,25 +103,37 @@ def gate_chunked(out, q, k, v, causal: bool = False, sm_scale: float | None = No
                  budget_bytes: int = DEFAULT_BUDGET_BYTES) -> dict:
     """TriBench's check_correctness (correctness.py:41-103) of ``out`` against the packs' ``ref``,
     computed chunk by chunk. Returns passed, atol, rtol, max_abs_err, max_rel_err, plus the
-    number of elements outside the tolerance (``n_fail``) and the element count."""
+    number of elements outside the tolerance (``n_fail``), the element count and the HND index
+    (b, h, row, channel) of the element furthest outside the tolerance, or closest to it when all
+    pass (``worst``: the largest |ref - out| - (atol + rtol |out|))."""
     atol, rtol = tolerance(dtype_str, atol, rtol, per_dtype)
     qh, kh, vh, oh = (_hnd(t, tensor_layout) for t in (q, k, v, out))
     if oh.shape != qh.shape:
         raise ValueError(f"output shape {tuple(out.shape)} != query shape {tuple(q.shape)}")
     scale = qh.shape[-1] ** -0.5 if sm_scale is None else sm_scale
     dev = oh.device
+    chunks = list(_chunks(qh, kh, causal, budget_bytes))
     max_abs = torch.zeros((), dtype=torch.float32, device=dev)
+    # per chunk: the largest excess |ref - out| - (atol + rtol |out|) and its flat index
+    worst = torch.zeros(len(chunks), dtype=torch.float32, device=dev)
+    where = torch.zeros(len(chunks), dtype=torch.int64, device=dev)
     max_rel = torch.zeros((), dtype=torch.float32, device=dev)
     n_fail = torch.zeros((), dtype=torch.int64, device=dev)
     with torch.no_grad():
-        for b, h, r0, r1 in _chunks(qh, kh, causal, budget_bytes):
+        for i, (b, h, r0, r1) in enumerate(chunks):
             ref = _ref_rows(qh, kh, vh, b, h, r0, r1, causal, scale).float()
             tri = oh[b, h, r0:r1].float()
             diff = (ref - tri).abs()
             # NaN propagates through max as in the unchunked reductions
             max_abs = torch.maximum(max_abs, diff.max())
+            worst[i], where[i] = (diff - (atol + rtol * tri.abs())).flatten().max(0)
             max_rel = torch.maximum(max_rel, (diff / ref.abs().clamp(min=1e-20)).max())
             n_fail += (~torch.isclose(ref, tri, atol=atol, rtol=rtol)).sum()
     n_fail = int(n_fail.item())
+    ci = int(worst.argmax().item()) if chunks else 0
+    b, h, r0, _ = chunks[ci] if chunks else (0, 0, 0, 0)
+    flat = int(where[ci].item()) if chunks else 0
+    D = qh.shape[-1]
     return {"passed": n_fail == 0, "atol": atol, "rtol": rtol, "max_abs_err": max_abs.item(),
-            "max_rel_err": max_rel.item(), "n_fail": n_fail, "numel": out.numel()}
+            "max_rel_err": max_rel.item(), "n_fail": n_fail, "numel": out.numel(),
+            "worst": (b, h, r0 + flat // D, flat % D)}
