@@ -441,7 +441,8 @@ def main():
             pg.barrier()
 
     # one wave = pre-pass + attention over a range of heads: the two C calls sage_run makes
-    # (sage_prepass, then sage_attn_fwd), split so that CUDA events bracket the attention kernel
+    # (sage_prepass, then sage_attn_fwd, or at head_dim 128 sage_attn_fwd_fused_q, which quantises
+    # Q itself), split so that CUDA events bracket the attention kernel
     def wave(a, b, ev=None):
         i, j = a - lo, b - lo
         pl = plans[j - i]
@@ -450,7 +451,7 @@ def main():
         pl.prepass(q[:, i:j], k[:, i:j], v[:, i:j])
         if ev is not None:
             ev[1].record(stream)
-        pl.attention(v[:, i:j], o[:, i:j])
+        pl.attention(v[:, i:j], o[:, i:j], q=q[:, i:j])
         if ev is not None:
             ev[2].record(stream)
 
@@ -549,9 +550,10 @@ def main():
                          f"{bf16} TF/s: QK^T at 2x (INT8), P.V at {'2x (FP8)' if pv == 'fp8' else '1x (fp16)'}",
                          "attn_ms": round(attn_avg, 4), "prepass_ms": round(statistics.mean(pre_ms), 4)},
             "prepass_roofline": {"bound": "hbm", "achieved": round(tb.prepass_bytes(dict(case, batch_size=1,
-                                 num_heads=hi - lo)) / (statistics.mean(pre_ms) * 1e-3) / 1e9, 1),
+                                 num_heads=hi - lo), fused_q=plan.fused_q) / (statistics.mean(pre_ms) * 1e-3) / 1e9, 1),
                                  "peak": peaks["hbm"], "unit": "GB/s",
-                                 "kernels": "kv_stats + kv_finalize + quant (3 launches)"},
+                                 "kernels": "kv_stats + kv_finalize + quant (3 launches)",
+                                 "q_quantised_in": "attention kernel" if plan.fused_q else "pre-pass"},
             "clocks": clk.summary(),
             "e2e": None if e2e_ms is None else {
                 "value": round(ops_total * args.e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT,

@@ -55,6 +55,14 @@ extern "C" {
 #define SAGE_FLAG_SMOOTH_K 1u  /* subtract K's per-channel token mean before quantising */
 #define SAGE_FLAG_KM_GIVEN 2u  /* with SMOOTH_K: k_mean is an input supplied by the caller
                                   (the reference's `km` argument) instead of being computed */
+#define SAGE_FLAG_FUSED_Q  4u  /* Q is quantised by the attention kernel itself (bit-identical
+                                  codes and output), not by the pre-pass: sage_run /
+                                  sage_run_varlen do this at head_dim 128 anyway and with this
+                                  flag at 64 too, q_i8 / q_scale then being optional outputs
+                                  (both NULL: not stored); sage_prepass with it skips Q, for
+                                  sage_attn_fwd_fused_q to follow */
+#define SAGE_FLAG_PREPASS_Q 8u /* sage_run / sage_run_varlen: quantise Q in the pre-pass even
+                                  at head_dim 128 (q_i8 / q_scale required) */
 
 /* Device-side status bits reported by sage_device_status(). */
 #define SAGE_DEV_TIMEOUT_PRODUCER 0x1
@@ -144,9 +152,26 @@ int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
                   int64_t seq_q, int64_t seq_kv, int64_t head_dim, void* stream);
 
 /*
+ * sage_attn_fwd with the Q quantisation inside the kernel: each CTA's softmax warps load their
+ * 128-row tiles of the caller's 16-bit q ({batch, head, seq} strides q_strides), quantise them
+ * exactly as sage_per_block_int8 does (multiplier sm_scale * log2 e, sm_scale <= 0 meaning
+ * head_dim^-0.5) straight into shared memory, and attend. q_i8_out / q_scale_out, both NULL or
+ * both set, receive the codes and scales in sage_per_block_int8's layouts. This is the second
+ * half of sage_run at head_dim 128 (its first half: sage_prepass with SAGE_FLAG_FUSED_Q).
+ * Replaces per_block_int8's Q half + the _attn_fwd launch (triton_impl.py:62-72, 121-160).
+ */
+int sage_attn_fwd_fused_q(const void* q, const int64_t q_strides[3], float sm_scale, const int8_t* k_i8,
+                          const float* k_scale, const void* v, const int64_t v_strides[3], const float* v_scale,
+                          void* o, const int64_t o_strides[3], int dtype, int pv_mode, int causal, int64_t batch,
+                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                          int8_t* q_i8_out, float* q_scale_out, void* stream);
+
+/*
  * The pre-pass half of sage_run on its own: K smoothing statistics, INT8 Q/K and (for
  * SAGE_PV_FP8) e4m3 V, in the same launches sage_run makes. Together with sage_attn_fwd it
- * is exactly sage_run; callers use the split to time or overlap the two halves.
+ * is exactly sage_run at head_dim 64; with SAGE_FLAG_FUSED_Q it leaves Q out (q_i8 / q_scale
+ * may be NULL) and together with sage_attn_fwd_fused_q is exactly sage_run at head_dim 128.
+ * Callers use the split to time or overlap the two halves.
  * Replaces per_block_int8 + v.to(float16) of run_sage_attn (triton_impl.py:171-173, 189).
  */
 int sage_prepass(const void* q, const void* k, const void* v, int dtype,
@@ -163,7 +188,10 @@ int sage_prepass(const void* q, const void* k, const void* v, int dtype,
  * Replaces run_sage_attn(q, k, v, causal, sm_scale) — kernels/sage_attn/triton_impl.py:162-200.
  * The caller provides every intermediate buffer listed at the top of this header
  * (v_fp8/v_scale only for SAGE_PV_FP8, k_mean only with SAGE_FLAG_SMOOTH_K) and a workspace
- * of at least sage_workspace_bytes(...) bytes.
+ * of at least sage_workspace_bytes(...) bytes. At head_dim 128 (or with SAGE_FLAG_FUSED_Q) Q
+ * is quantised inside the attention kernel (sage_prepass with SAGE_FLAG_FUSED_Q, then
+ * sage_attn_fwd_fused_q) and q_i8 / q_scale are optional outputs; the result is bit-identical
+ * to the pre-pass route (sage_prepass + sage_attn_fwd).
  */
 int sage_run(const void* q, const void* k, const void* v, void* o, int dtype,
              int64_t batch, int64_t heads_q, int64_t heads_kv,

@@ -148,3 +148,27 @@ def test_flash_rejects_bad_arguments_before_any_cuda_call():
     assert call(q=ctypes.c_void_p(p.value + 4)) == N.SAGE_ERR_INVALID_ARG
     assert "aligned" in lib.sage_last_error().decode()
     assert call(q=None) == N.SAGE_ERR_INVALID_ARG
+
+
+def test_fused_q_makes_q_buffers_optional():
+    """Host-side validation (no device here): NULL q_i8 / q_scale are rejected unless Q is
+    quantised in the attention kernel."""
+    lib = N.load()
+    keep, p = _dummy()
+    s = N.strides3(8 * 128, 8 * 128, 128)
+
+    def run(flags, qi):
+        return lib.sage_run(p, p, p, p, N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 128, s, s, s, s, 0, 0.0, N.SAGE_PV_16BIT,
+                            flags, qi, qi, p, p, None, None, None, None, 0, None)
+
+    assert run(N.SAGE_FLAG_PREPASS_Q, None) == N.SAGE_ERR_INVALID_ARG and "NULL" in lib.sage_last_error().decode()
+    # fused (the flag, or head_dim 128 by default): the arguments pass validation and the call
+    # then stops at the missing device
+    assert run(N.SAGE_FLAG_FUSED_Q, None) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)
+    assert run(0, None) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)
+    assert run(N.SAGE_FLAG_FUSED_Q | N.SAGE_FLAG_PREPASS_Q, p) == N.SAGE_ERR_INVALID_ARG
+    # sage_prepass needs q_i8 / q_scale unless told that Q is left to the attention kernel
+    pre = lambda flags: lib.sage_prepass(p, p, p, N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 128, s, s, s, 0.0,
+                                         N.SAGE_PV_16BIT, flags, None, None, p, p, None, None, None, None, 0, None)
+    assert pre(0) == N.SAGE_ERR_INVALID_ARG
+    assert pre(N.SAGE_FLAG_FUSED_Q) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)

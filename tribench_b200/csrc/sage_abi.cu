@@ -243,12 +243,12 @@ int prepass_dispatch(int dtype, int64_t D, const void* q, const void* k, const v
 }
 
 // ---------------------------------------------------------------- attention launch
-template <int D, int PV, bool OBF16, bool FLASH = false>
+template <int D, int PV, bool OBF16, bool FLASH = false, bool FQ = false>
 int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const sage::AttnParams& p,
                 cudaStream_t st) {
   constexpr int QT = 2;
   using C = sage::AttnCfg<D, PV, QT, FLASH>;
-  auto kern = sage::sage_attn_kernel<D, PV, QT, OBF16, FLASH>;
+  auto kern = sage::sage_attn_kernel<D, PV, QT, OBF16, FLASH, FQ>;
   if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), C::SMEM_BYTES)) return rc;
   dim3 grid((unsigned)p.n_m_ctas, (unsigned)p.Hq, (unsigned)p.B);
   kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
@@ -274,21 +274,52 @@ void set_seq_params(sage::AttnParams& p, const Varlen* vl, const int64_t* os, in
   if (vl) { p.cu_q = vl->cu_q; p.cu_k = vl->cu_k; p.q_tokens = (int)vl->q_tokens; p.k_tokens = (int)vl->k_tokens; }
 }
 
+// The INT8 attention instantiations: head_dim x P.V mode x output type, with Q quantised by the
+// pre-pass (FQ = false) or inside the kernel (FQ = true).
+template <bool FQ>
+int attn_dispatch(int64_t D, bool fp8, bool obf, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                  const sage::AttnParams& p, cudaStream_t st) {
+  if (D == 128) {
+    if (fp8) return obf ? launch_attn<128, sage::kPvE4M3, true, false, FQ>(tq, tk, tv, p, st)
+                        : launch_attn<128, sage::kPvE4M3, false, false, FQ>(tq, tk, tv, p, st);
+    return obf ? launch_attn<128, sage::kPvBF16, true, false, FQ>(tq, tk, tv, p, st)
+               : launch_attn<128, sage::kPvF16, false, false, FQ>(tq, tk, tv, p, st);
+  }
+  if (fp8) return obf ? launch_attn<64, sage::kPvE4M3, true, false, FQ>(tq, tk, tv, p, st)
+                      : launch_attn<64, sage::kPvE4M3, false, false, FQ>(tq, tk, tv, p, st);
+  return obf ? launch_attn<64, sage::kPvBF16, true, false, FQ>(tq, tk, tv, p, st)
+             : launch_attn<64, sage::kPvF16, false, false, FQ>(tq, tk, tv, p, st);
+}
+
+// Q quantised inside the attention kernel instead of by the pre-pass: the caller's 16-bit Q,
+// its {batch, head, seq} strides and multiplier; the codes / scales are also stored where
+// q_i8_out / q_scale_out are not NULL.
+struct FusedQ {
+  const void* q;
+  const int64_t* qs;
+  float q_mult;
+  int8_t* q_i8_out;
+  float* q_scale_out;
+};
+
 int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale, const void* v,
               const int64_t* vs, const float* v_scale, void* o, const int64_t* os, int dtype, int pv_mode, int causal,
               int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, cudaStream_t st,
-              const Varlen* vl = nullptr) {
+              const Varlen* vl = nullptr, const FusedQ* fq = nullptr) {
   const bool fp8 = pv_mode == SAGE_PV_FP8;
   // rows of the token axis and batch extent of every tensor map (packed sequences: one batch)
   const int64_t rq = vl ? vl->q_tokens : Sq, rk = vl ? vl->k_tokens : Skv, nb = vl ? 1 : B;
   CUtensorMap tq, tk, tv;
   const CUtensorMapSwizzle swqk = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  if (int rc = encode_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q_i8, D, rq, Hq, nb, D, rq * D, Hq * rq * D,
-                         (uint32_t)D, 128, swqk))
-    return rc;
   if (int rc = encode_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k_i8, D, rk, Hkv, nb, D, rk * D, Hkv * rk * D,
                          (uint32_t)D, 128, swqk))
     return rc;
+  if (fq) {
+    tq = tk;  // not read: the kernel loads Q itself
+  } else if (int rc = encode_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q_i8, D, rq, Hq, nb, D, rq * D, Hq * rq * D,
+                                (uint32_t)D, 128, swqk)) {
+    return rc;
+  }
   if (fp8) {
     if (int rc = encode_4d(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, v, D, rk, Hkv, nb, D, rk * D, Hkv * rk * D,
                            (uint32_t)D, 128, swqk))
@@ -303,17 +334,14 @@ int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, cons
   sage::AttnParams p{};
   p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.o = o;
   set_seq_params(p, vl, os, B, Hq, Hkv, Sq, Skv, causal);
-  const bool obf = dtype == SAGE_DTYPE_BF16;
-  if (D == 128) {
-    if (fp8) return obf ? launch_attn<128, sage::kPvE4M3, true>(tq, tk, tv, p, st)
-                        : launch_attn<128, sage::kPvE4M3, false>(tq, tk, tv, p, st);
-    return obf ? launch_attn<128, sage::kPvBF16, true>(tq, tk, tv, p, st)
-               : launch_attn<128, sage::kPvF16, false>(tq, tk, tv, p, st);
+  if (fq) {
+    p.q_src = fq->q;
+    p.q_sb = vl ? 0 : fq->qs[0]; p.q_sh = fq->qs[1]; p.q_ss = fq->qs[2];
+    p.q_mult = fq->q_mult;
+    p.q_i8_out = fq->q_i8_out; p.q_scale_out = fq->q_scale_out;
   }
-  if (fp8) return obf ? launch_attn<64, sage::kPvE4M3, true>(tq, tk, tv, p, st)
-                      : launch_attn<64, sage::kPvE4M3, false>(tq, tk, tv, p, st);
-  return obf ? launch_attn<64, sage::kPvBF16, true>(tq, tk, tv, p, st)
-             : launch_attn<64, sage::kPvF16, false>(tq, tk, tv, p, st);
+  const bool obf = dtype == SAGE_DTYPE_BF16;
+  return fq ? attn_dispatch<true>(D, fp8, obf, tq, tk, tv, p, st) : attn_dispatch<false>(D, fp8, obf, tq, tk, tv, p, st);
 }
 
 // flash_attn pack: the same pipeline on fp16/bf16 Q and K (no pre-pass)
@@ -508,23 +536,64 @@ int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, 
                    heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream));
 }
 
+int sage_attn_fwd_fused_q(const void* q, const int64_t q_strides[3], float sm_scale, const int8_t* k_i8,
+                          const float* k_scale, const void* v, const int64_t v_strides[3], const float* v_scale,
+                          void* o, const int64_t o_strides[3], int dtype, int pv_mode, int causal, int64_t batch,
+                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                          int8_t* q_i8_out, float* q_scale_out, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
+    return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
+  if (causal && seq_q != seq_kv)
+    return fail(SAGE_ERR_INVALID_ARG, "causal attention needs seq_q == seq_kv (got %lld, %lld)", (long long)seq_q,
+                (long long)seq_kv);
+  if (int rc = check_strides("q", q_strides)) return rc;
+  if (int rc = check_strides("o", o_strides)) return rc;
+  if (pv_mode == SAGE_PV_16BIT) {
+    if (int rc = check_strides("v", v_strides)) return rc;
+  } else if (!v_scale) {
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs v_scale");
+  }
+  if (!q || !k_i8 || !k_scale || !v || !o || (!q_i8_out != !q_scale_out))
+    return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q) || !aligned16(k_i8) || !aligned16(v) || !aligned16(o) || (q_i8_out && !aligned16(q_i8_out)))
+    return fail(SAGE_ERR_INVALID_ARG, "q/k_i8/v/o/q_i8_out must be 16-byte aligned");
+  if (int rc = check_arch()) return rc;
+  const FusedQ fq{q, q_strides, q_multiplier(sm_scale, head_dim), q_i8_out, q_scale_out};
+  return attn_impl(nullptr, nullptr, k_i8, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal,
+                   batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream), nullptr, &fq);
+}
+
 namespace {
+// Where sage_run / sage_run_varlen quantise Q: inside the attention kernel at head_dim 128
+// (H8K 1.817 -> 1.774 ms per call: the pre-pass no longer reads Q and writes its INT8 copy) or
+// with SAGE_FLAG_FUSED_Q, else in the pre-pass (at head_dim 64 the fused kernel was 3 % slower).
+// SAGE_FLAG_PREPASS_Q keeps Q in the pre-pass at head_dim 128.
+bool fused_q_for(unsigned flags, int64_t head_dim) {
+  if (flags & SAGE_FLAG_PREPASS_Q) return false;
+  return (flags & SAGE_FLAG_FUSED_Q) != 0 || head_dim == 128;
+}
+
 // Shared validation of sage_prepass / sage_run; returns SAGE_OK or the failing status.
 int check_run_args(const void* q, const void* k, const void* v, int dtype, int64_t batch, int64_t heads_q,
                    int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim, const int64_t* q_strides,
                    const int64_t* k_strides, const int64_t* v_strides, int pv_mode, unsigned flags,
                    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale,
                    const float* k_mean, const uint8_t* v_fp8, const float* v_scale, const void* workspace,
-                   size_t workspace_bytes) {
+                   size_t workspace_bytes, bool fused_q) {
   if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
   if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
+  if ((flags & SAGE_FLAG_FUSED_Q) && (flags & SAGE_FLAG_PREPASS_Q))
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_FUSED_Q and SAGE_FLAG_PREPASS_Q exclude each other");
   if (int rc = check_strides("q", q_strides)) return rc;
   if (int rc = check_strides("k", k_strides)) return rc;
   if (int rc = check_strides("v", v_strides)) return rc;
-  if (!q || !k || !v || !q_i8 || !q_scale || !k_i8 || !k_scale)
+  // where Q is quantised in the attention kernel its codes / scales are optional outputs
+  if (!q || !k || !v || !k_i8 || !k_scale || (!fused_q && (!q_i8 || !q_scale)) || (!q_i8 != !q_scale))
     return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(q_i8) || !aligned16(k_i8))
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (q_i8 && !aligned16(q_i8)) || !aligned16(k_i8))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/v/q_i8/k_i8 must be 16-byte aligned");
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
   const bool fp8 = pv_mode == SAGE_PV_FP8;
@@ -548,16 +617,17 @@ int sage_prepass(const void* q, const void* k, const void* v, int dtype, int64_t
   g_last_error.clear();
   if (int rc = check_run_args(q, k, v, dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, q_strides,
                               k_strides, v_strides, pv_mode, flags, q_i8, q_scale, k_i8, k_scale, k_mean, v_fp8,
-                              v_scale, workspace, workspace_bytes))
+                              v_scale, workspace, workspace_bytes, (flags & SAGE_FLAG_FUSED_Q) != 0))
     return rc;
   if (int rc = check_arch()) return rc;
   const bool fp8 = pv_mode == SAGE_PV_FP8;
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
-  return prepass_dispatch(dtype, head_dim, q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv, seq_q, seq_kv,
-                          q_strides, k_strides, v_strides, q_multiplier(sm_scale, head_dim), smooth,
-                          smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, q_i8, q_scale, k_i8, k_scale, k_mean,
-                          fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace,
-                          static_cast<cudaStream_t>(stream));
+  const bool fused_q = (flags & SAGE_FLAG_FUSED_Q) != 0;  // Q is left to sage_attn_fwd_fused_q
+  return prepass_dispatch(dtype, head_dim, fused_q ? nullptr : q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv,
+                          seq_q, seq_kv, q_strides, k_strides, v_strides, q_multiplier(sm_scale, head_dim), smooth,
+                          smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, fused_q ? nullptr : q_i8,
+                          fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr,
+                          fp8 ? v_scale : nullptr, workspace, static_cast<cudaStream_t>(stream));
 }
 
 int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch, int64_t heads_q,
@@ -569,7 +639,7 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
   g_last_error.clear();
   if (int rc = check_run_args(q, k, v, dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, q_strides,
                               k_strides, v_strides, pv_mode, flags, q_i8, q_scale, k_i8, k_scale, k_mean, v_fp8,
-                              v_scale, workspace, workspace_bytes))
+                              v_scale, workspace, workspace_bytes, fused_q_for(flags, head_dim)))
     return rc;
   if (causal && seq_q != seq_kv)
     return fail(SAGE_ERR_INVALID_ARG, "causal attention needs seq_q == seq_kv (got %lld, %lld)", (long long)seq_q,
@@ -580,14 +650,20 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool fp8 = pv_mode == SAGE_PV_FP8;
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
-  if (int rc = prepass_dispatch(dtype, head_dim, q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv, seq_q, seq_kv,
-                                q_strides, k_strides, v_strides, q_multiplier(sm_scale, head_dim), smooth,
-                                smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, q_i8, q_scale, k_i8, k_scale, k_mean,
-                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st))
+  // Q quantised by the attention kernel itself (the pre-pass then handles K and V only) at
+  // head_dim 128 or with SAGE_FLAG_FUSED_Q; the codes and output are identical either way
+  const bool fused_q = fused_q_for(flags, head_dim);
+  const float q_mult = q_multiplier(sm_scale, head_dim);
+  if (int rc = prepass_dispatch(dtype, head_dim, fused_q ? nullptr : q, k, fp8 ? v : nullptr, batch, heads_q,
+                                heads_kv, seq_q, seq_kv, q_strides, k_strides, v_strides, q_mult, smooth,
+                                smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, fused_q ? nullptr : q_i8,
+                                fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr,
+                                fp8 ? v_scale : nullptr, workspace, st))
     return rc;
+  const FusedQ fq{q, q_strides, q_mult, q_i8, q_scale};
   return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, v_strides,
                    fp8 ? v_scale : nullptr, o, o_strides, dtype, pv_mode, causal, batch, heads_q, heads_kv, seq_q,
-                   seq_kv, head_dim, st);
+                   seq_kv, head_dim, st, nullptr, fused_q ? &fq : nullptr);
 }
 
 int sage_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,
@@ -687,9 +763,13 @@ int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dt
   if (int rc = packed_strides("o", o_strides, os)) return rc;
   if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
-  if (!q || !k || !v || !o || !q_i8 || !q_scale || !k_i8 || !k_scale)
+  if ((flags & SAGE_FLAG_FUSED_Q) && (flags & SAGE_FLAG_PREPASS_Q))
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_FUSED_Q and SAGE_FLAG_PREPASS_Q exclude each other");
+  const bool fused_q = fused_q_for(flags, head_dim);
+  if (!q || !k || !v || !o || !k_i8 || !k_scale || (!fused_q && (!q_i8 || !q_scale)) || (!q_i8 != !q_scale))
     return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(q_i8) || !aligned16(k_i8))
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (q_i8 && !aligned16(q_i8)) ||
+      !aligned16(k_i8))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o/q_i8/k_i8 must be 16-byte aligned");
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
   const bool fp8 = pv_mode == SAGE_PV_FP8;
@@ -703,14 +783,16 @@ int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dt
   if (int rc = check_arch()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Varlen vl{cu_seqlens_q, cu_seqlens_kv, total_q, total_kv};
-  if (int rc = prepass_dispatch(dtype, head_dim, q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv, max_seq_q,
-                                max_seq_kv, qs, ks, vs, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8,
-                                q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr,
-                                workspace, st, &vl))
+  const float q_mult = q_multiplier(sm_scale, head_dim);
+  if (int rc = prepass_dispatch(dtype, head_dim, fused_q ? nullptr : q, k, fp8 ? v : nullptr, batch, heads_q,
+                                heads_kv, max_seq_q, max_seq_kv, qs, ks, vs, q_mult, smooth, km_given,
+                                fused_q ? nullptr : q_i8, fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean,
+                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st, &vl))
     return rc;
+  const FusedQ fq{q, qs, q_mult, q_i8, q_scale};
   return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, vs,
                    fp8 ? v_scale : nullptr, o, os, dtype, pv_mode, causal, batch, heads_q, heads_kv, max_seq_q,
-                   max_seq_kv, head_dim, st, &vl);
+                   max_seq_kv, head_dim, st, &vl, fused_q ? &fq : nullptr);
 }
 
 int sage_flash_attn_varlen_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,

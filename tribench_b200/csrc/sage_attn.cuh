@@ -30,6 +30,9 @@
 //     PV_t(j-1) to finish (pvdone) before it writes P_t(j) or rescales O_t.
 #pragma once
 
+#include <type_traits>
+
+#include "sage_quant.cuh"
 #include "sage_seq.cuh"
 #include "sm100_ptx.cuh"
 
@@ -55,6 +58,15 @@ struct AttnParams {
   int n_m_ctas;              // CTAs along the query axis
   unsigned long long wait_limit_ns;
   float qk_scale;            // FLASH only: sm_scale * log2(e)
+  // Q quantised inside the kernel (nullable): q_src is the caller's 16-bit Q with element strides
+  // q_sb/q_sh/q_ss (batch, head, token), quantised per 128-row tile exactly as the pre-pass
+  // does (multiplier q_mult). q_i8_out / q_scale_out (nullable) receive the codes and scales in
+  // the pre-pass's layouts.
+  const void* q_src;
+  int64_t q_sb, q_sh, q_ss;
+  float q_mult;
+  int8_t* q_i8_out;
+  float* q_scale_out;
 };
 
 template <int D, int PV, int QT, bool FLASH = false>
@@ -82,7 +94,8 @@ struct AttnCfg {
   // q, kfull/vfull/kvempty per stage, sfull/phalf/pfull/odone/sload/pvdone per query tile
   static constexpr int NUM_BARS = 1 + 3 * NS + 6 * QT;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-  static constexpr int SMEM_USED = OFF_MISC + 16;
+  static constexpr int OFF_QRED = OFF_MISC + 16;  // fused Q quantisation: per-warp maxima
+  static constexpr int SMEM_USED = OFF_QRED + 16 * QT;
   // Pad to > half of the SM's shared memory so that exactly one CTA is resident per SM:
   // each CTA allocates all 512 TMEM columns when QT == 2.
   static constexpr int SMEM_MIN = (QT == 2) ? 118 * 1024 : 0;
@@ -168,7 +181,73 @@ __device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint3
   }
 }
 
-template <int D, int PV, int QT, bool OBF16, bool FLASH>
+// Q quantisation inside the attention kernel. The 128 threads of warpgroup t quantise query
+// tile t (one 128-row scale block): thread r loads the 16-byte pieces r, r + 128, r + 256, ...
+// of the tile in row-major order (consecutive threads read consecutive bytes of the caller's
+// rows), the warpgroup takes the tile's absmax, and each piece's eight INT8 codes go straight
+// into the tile's shared-memory image in the layout the TMA load would have produced (K-major,
+// 128-byte swizzle for 128-byte rows, 64-byte swizzle for 64-byte rows). The arithmetic is the
+// pre-pass's (quant_block_role in sage_quant.cuh), so codes and scale are bit-identical to it.
+// Every softmax thread arrives on bar_q after a proxy fence, so the MMA warp may read the tile.
+// Returns the tile's scale.
+template <class C, int D, bool OBF16>
+__device__ __forceinline__ float fused_q_tile(const AttnParams& p, uint8_t* qtile, float* red, int t, int r,
+                                              const SeqSpan& sq, int b, int h, int tile, uint64_t* bar_q) {
+  using T = typename std::conditional<OBF16, __nv_bfloat16, __half>::type;
+  constexpr int PR = D / 8;              // 16-byte pieces (8 elements) per row
+  constexpr int NP = C::BM * PR / 128;   // pieces per thread
+  const int row0 = tile * C::BM;
+  const char* base = reinterpret_cast<const char*>(p.q_src) +
+                     ((int64_t)sq.batch * p.q_sb + (int64_t)h * p.q_sh + (int64_t)(sq.base + row0) * p.q_ss) * 2;
+  uint4 raw[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int pc = i * 128 + r, row = pc / PR, c = pc % PR;
+    raw[i] = (row0 + row < sq.len) ? ldg_nc_v4(base + (int64_t)row * p.q_ss * 2 + c * 16) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) amax = fmaxf(amax, Half8<T>::absmax(raw[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((r & 31) == 0) red[r >> 5] = amax;
+  // the 128 threads of warpgroup t (named barriers 3 and 4; immediate ids keep the count known)
+  if (t == 0) asm volatile("bar.sync 3, 128;" ::: "memory");
+  else asm volatile("bar.sync 4, 128;" ::: "memory");
+  amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const float scale = __fdiv_rn(__fmul_rn(amax, p.q_mult), 127.0f);
+  const float rcp = __frcp_rn(scale);
+  const float2 s2 = make_float2(scale, scale), ns2 = make_float2(-scale, -scale), r2 = make_float2(rcp, rcp);
+  const float2 mult2 = make_float2(p.q_mult, p.q_mult);
+  int8_t* dump = nullptr;
+  if (p.q_i8_out != nullptr) {
+    const size_t first = p.cu_q ? (size_t)h * p.q_tokens + sq.base : ((size_t)b * p.Hq + h) * (size_t)sq.len;
+    dump = p.q_i8_out + (first + row0) * D;
+  }
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int pc = i * 128 + r, row = pc / PR, c = pc % PR;
+    float f[8];
+    Half8<T>::to_float(raw[i], f);
+    int qv[8];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2)
+      quant_two(fmul2(make_float2(f[e], f[e + 1]), mult2), s2, ns2, r2, qv[e], qv[e + 1]);
+    const uint2 codes = make_uint2(pack4_lo_bytes(qv[0], qv[1], qv[2], qv[3]), pack4_lo_bytes(qv[4], qv[5], qv[6], qv[7]));
+    // 16-byte swizzle unit c/2 of the row, half c%2 of it
+    const int sw = (D == 128) ? ((c >> 1) ^ (row & 7)) : ((c >> 1) ^ ((row >> 1) & 3));
+    *reinterpret_cast<uint2*>(qtile + row * D + sw * 16 + (c & 1) * 8) = codes;
+    if (dump && row0 + row < sq.len) *reinterpret_cast<uint2*>(dump + row * D + c * 8) = codes;
+  }
+  if (p.q_scale_out != nullptr && r == 0 && row0 < sq.len) p.q_scale_out[((size_t)b * p.Hq + h) * p.nqb + tile] = scale;
+  fence_proxy_async_smem();  // the codes are read by tcgen05.mma (async proxy)
+  mbar_arrive(bar_q);
+  return scale;
+}
+
+// FQ: Q arrives as the caller's 16-bit tensor and is quantised by the softmax warps
+// (fused_q_tile); a separate instantiation, so the default kernel carries none of that code.
+template <int D, int PV, int QT, bool OBF16, bool FLASH, bool FQ = false>
 __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -215,7 +294,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
   }
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_q, 1);
+    mbar_init(bar_q, FQ ? 128 * QT : 1);  // fused Q: every softmax thread arrives
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(bar_kfull + s, 1);
       mbar_init(bar_vfull + s, 1);
@@ -260,13 +339,15 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
     // ------------------------------------------------------------ TMA producer
     SAGE_T_DECL
     if (elect_one() && nkv_max > 0) {
-      mbar_arrive_expect_tx(bar_q, QT * C::Q_TILE);
+      if constexpr (!FQ) {
+        mbar_arrive_expect_tx(bar_q, QT * C::Q_TILE);
 #pragma unroll
-      for (int t = 0; t < QT; ++t)
+        for (int t = 0; t < QT; ++t)
 #pragma unroll
-        for (int x = 0; x < C::QK_ATOMS; ++x)
-          tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE + x * (C::BM * 128), &tmQ, bar_q, x * C::QK_BOX,
-                      sq.base + (m_cta * QT + t) * C::BM, h, sq.batch);
+          for (int x = 0; x < C::QK_ATOMS; ++x)
+            tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE + x * (C::BM * 128), &tmQ, bar_q, x * C::QK_BOX,
+                        sq.base + (m_cta * QT + t) * C::BM, h, sq.batch);
+      }
       for (int j = 0; j < nkv_max; ++j) {
         const int s = j % C::NS;
         SAGE_T_MARK(1)
@@ -401,7 +482,15 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
     const uint32_t s_tmem = tmem_base + lane_base + 256 * t;
     const uint32_t o_tmem = s_tmem + 128;
     const int n = nkv[t];
-    const float qs = (!FLASH && n > 0) ? p.q_scale[((size_t)b * p.Hq + h) * p.nqb + r0 / C::BM] : 0.0f;
+    float qs;
+    if constexpr (FQ) {
+      static_assert(!FLASH && QT == 2, "fused Q quantisation: INT8 path, two query tiles");
+      qs = fused_q_tile<C, D, OBF16>(p, smem + C::OFF_Q + t * C::Q_TILE,
+                                     reinterpret_cast<float*>(smem + C::OFF_QRED) + 4 * t, t, row_in_tile, sq, b, h,
+                                     r0 / C::BM, bar_q);
+    } else {
+      qs = (!FLASH && n > 0) ? p.q_scale[((size_t)b * p.Hq + h) * p.nqb + r0 / C::BM] : 0.0f;
+    }
     const float* ksp = FLASH ? nullptr : p.k_scale + ((size_t)b * p.Hkv + hkv) * p.nkb;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;

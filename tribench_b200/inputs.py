@@ -119,15 +119,19 @@ def estimate(case: dict) -> dict:
             "ops_qk": 2 * B * H * pairs * D, "ops_pv": 2 * B * H * pairs * D}
 
 
-def prepass_bytes(case: dict) -> int:
+def prepass_bytes(case: dict, fused_q: bool = False) -> int:
     """Algorithmic HBM bytes of the pre-pass: read Q and K at 2 B/elt, write int8 Q/K, fp32
-    scales and the fp32 K mean; with FP8 P.V also read V (2 B) and write e4m3 V (1 B) + scales."""
+    scales and the fp32 K mean; with FP8 P.V also read V (2 B) and write e4m3 V (1 B) + scales.
+    ``fused_q``: Q is quantised by the attention kernel, so the pre-pass moves K's bytes only."""
     B = case.get("batch_size", 8)
     H = case.get("num_heads", 16)
     S = case.get("seq_len", 4096)
     D = case.get("head_dim", 64)
     n = B * H * S * D
-    b = 2 * (3 * n) + 4 * (B * H * math.ceil(S / 128) + B * H * math.ceil(S / 64) + B * H * D)
+    if fused_q:
+        b = 3 * n + 4 * (B * H * math.ceil(S / 64) + B * H * D)
+    else:
+        b = 2 * (3 * n) + 4 * (B * H * math.ceil(S / 128) + B * H * math.ceil(S / 64) + B * H * D)
     if case.get("pv") == "fp8":
         b += 3 * n + 4 * B * H * D
     return b

@@ -180,22 +180,28 @@ class SagePlan:
     """Preallocated intermediates for repeated calls on one shape (no per-call allocation).
 
     ``plan.run(q, k, v, o)`` is one ``sage_run`` C call: pre-pass kernels + attention kernel.
+    ``fused_q``: where Q is quantised — True: inside the attention kernel (the pre-pass handles
+    K and V only; no INT8 Q buffer unless ``keep_q_int8``), False: in the pre-pass, None: as
+    sage_run chooses (inside the kernel at head_dim 128, the faster route there; in the pre-pass
+    at 64). Codes and output are bit-identical either way.
     """
 
     def __init__(self, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, dtype, device, *, pv="16bit",
-                 smooth_k=True, causal=False, sm_scale=None):
+                 smooth_k=True, causal=False, sm_scale=None, fused_q=None, keep_q_int8=False):
         if dtype not in _DTYPES:
             raise TypeError(f"dtype must be float16 or bfloat16, got {dtype}")
         self.shape = (batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)
         self.dtype, self.device = dtype, torch.device(device)
         self.pv_mode = _PV[pv]
         self.flags = N.SAGE_FLAG_SMOOTH_K if smooth_k else 0
+        self.fused_q = (head_dim == 128) if fused_q is None else bool(fused_q)
         self.causal, self.sm_scale = bool(causal), sm_scale
         B, Hq, Hkv, Sq, Skv, D = self.shape
         dev = self.device
+        want_q = not self.fused_q or keep_q_int8
         self.quant = SageQuant(
-            q_int8=torch.empty((B, Hq, Sq, D), dtype=torch.int8, device=dev),
-            q_scale=torch.empty((B, Hq, (Sq + 127) // 128), dtype=torch.float32, device=dev),
+            q_int8=torch.empty((B, Hq, Sq, D), dtype=torch.int8, device=dev) if want_q else None,
+            q_scale=torch.empty((B, Hq, (Sq + 127) // 128), dtype=torch.float32, device=dev) if want_q else None,
             k_int8=torch.empty((B, Hkv, Skv, D), dtype=torch.int8, device=dev),
             k_scale=torch.empty((B, Hkv, (Skv + 63) // 64), dtype=torch.float32, device=dev),
             k_mean=torch.empty((B, Hkv, D), dtype=torch.float32, device=dev) if smooth_k else None,
@@ -206,7 +212,8 @@ class SagePlan:
         self.ws = torch.empty(max(self.ws_bytes, 1), dtype=torch.uint8, device=dev)
 
     def prepass(self, q, k, v, tensor_layout="HND"):
-        """The pre-pass half of run() (sage_prepass): fills self.quant from q, k (and v for FP8)."""
+        """The pre-pass half of run() (sage_prepass): fills self.quant from k (and v for FP8), and
+        from q unless the plan quantises Q in the attention kernel."""
         B, Hq, Hkv, Sq, Skv, D = self.shape
         *_, qs = _dims(q, tensor_layout)
         *_, ks = _dims(k, tensor_layout)
@@ -215,16 +222,38 @@ class SagePlan:
         rc = N.load().sage_prepass(
             _vp(q), _vp(k), _vp(v), _DTYPES[self.dtype], B, Hq, Hkv, Sq, Skv, D, N.strides3(*qs), N.strides3(*ks),
             N.strides3(*vs), ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)), self.pv_mode,
-            self.flags, _vp(qd.q_int8), _vp(qd.q_scale), _vp(qd.k_int8), _vp(qd.k_scale), _vp(qd.k_mean),
+            self.flags | (N.SAGE_FLAG_FUSED_Q if self.fused_q else 0),
+            _vp(None if self.fused_q else qd.q_int8), _vp(None if self.fused_q else qd.q_scale), _vp(qd.k_int8),
+            _vp(qd.k_scale), _vp(qd.k_mean),
             _vp(qd.v_fp8), _vp(qd.v_scale), _vp(self.ws), self.ws_bytes, _stream_ptr(self.device))
         N.check("sage_prepass", rc)
         return self.quant
 
-    def attention(self, v, out, tensor_layout="HND"):
-        """The attention half of run() (sage_attn_fwd) over self.quant."""
+    def attention(self, v, out, tensor_layout="HND", q=None):
+        """The attention half of run() over self.quant: sage_attn_fwd, or sage_attn_fwd_fused_q
+        (which needs ``q``) when the plan quantises Q in the attention kernel."""
         pv = "fp8" if self.pv_mode == N.SAGE_PV_FP8 else "16bit"
-        return attn_fwd(self.quant, v, self.causal, pv=pv, out_dtype=self.dtype, tensor_layout=tensor_layout,
-                        out=out)
+        if not self.fused_q:
+            return attn_fwd(self.quant, v, self.causal, pv=pv, out_dtype=self.dtype, tensor_layout=tensor_layout,
+                            out=out)
+        if q is None:
+            raise ValueError("this plan quantises Q inside the attention kernel: pass q")
+        B, Hq, Hkv, Sq, Skv, D = self.shape
+        qd = self.quant
+        *_, qs = _dims(q, tensor_layout)
+        *_, os_ = _dims(out, tensor_layout)
+        if self.pv_mode == N.SAGE_PV_FP8:
+            vv, vs = qd.v_fp8, (Skv * D * Hkv, Skv * D, D)
+        else:
+            vv = v
+            *_, vs = _dims(v, tensor_layout)
+        rc = N.load().sage_attn_fwd_fused_q(
+            _vp(q), N.strides3(*qs), ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)),
+            _vp(qd.k_int8), _vp(qd.k_scale), _vp(vv), N.strides3(*vs), _vp(qd.v_scale), _vp(out), N.strides3(*os_),
+            _DTYPES[self.dtype], self.pv_mode, int(self.causal), B, Hq, Hkv, Sq, Skv, D, _vp(qd.q_int8),
+            _vp(qd.q_scale), _stream_ptr(self.device))
+        N.check("sage_attn_fwd_fused_q", rc)
+        return out
 
     def cuda_graph(self, q, k, v, out, tensor_layout="HND") -> "SageGraph":
         """Capture run(q, k, v, out) into a CUDA graph (see SageGraph)."""
@@ -249,7 +278,8 @@ class SagePlan:
         rc = N.load().sage_run(
             _vp(q), _vp(k), _vp(v), _vp(out), _DTYPES[self.dtype], B, Hq, Hkv, Sq, Skv, D,
             N.strides3(*qs), N.strides3(*ks), N.strides3(*vs), N.strides3(*os_), int(self.causal),
-            ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)), self.pv_mode, self.flags,
+            ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)), self.pv_mode,
+            self.flags | (N.SAGE_FLAG_FUSED_Q if self.fused_q else N.SAGE_FLAG_PREPASS_Q),
             _vp(qd.q_int8), _vp(qd.q_scale), _vp(qd.k_int8), _vp(qd.k_scale), _vp(qd.k_mean), _vp(qd.v_fp8),
             _vp(qd.v_scale), _vp(self.ws), self.ws_bytes, _stream_ptr(self.device))
         N.check("sage_run", rc)
@@ -365,11 +395,12 @@ class HostPipeline:
 
 
 def run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=True, tensor_layout="HND",
-                  out=None):
+                  out=None, fused_q=None):
     """Drop-in for run_sage_attn (triton_impl.py:162-200) on sm_100a.
 
     q: [B, Hq, Sq, D], k/v: [B, Hkv, Skv, D] (HND; NHD with tensor_layout="NHD"), fp16 or bf16,
-    D in {64, 128}. Returns o with q's shape and dtype.
+    D in {64, 128}. Returns o with q's shape and dtype. ``fused_q``: where Q is quantised
+    (SagePlan; None = sage_run's choice); the output is bit-identical either way.
     """
     _check_tensor("q", q)
     for name, t in (("k", k), ("v", v)):
@@ -381,7 +412,7 @@ def run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=
     B, Hq, Sq, D, _ = _dims(q, tensor_layout)
     _, Hkv, Skv, _, _ = _dims(k, tensor_layout)
     plan = SagePlan(B, Hq, Hkv, Sq, Skv, D, q.dtype, q.device, pv=pv, smooth_k=smooth_k, causal=causal,
-                    sm_scale=sm_scale)
+                    sm_scale=sm_scale, fused_q=fused_q)
     with torch.cuda.device(q.device):
         return plan.run(q, k, v, out=out, tensor_layout=tensor_layout)
 
