@@ -61,8 +61,12 @@ extern "C" {
                                   flag at 64 too, q_i8 / q_scale then being optional outputs
                                   (both NULL: not stored); sage_prepass with it skips Q, for
                                   sage_attn_fwd_fused_q to follow */
-#define SAGE_FLAG_PREPASS_Q 8u /* sage_run / sage_run_varlen: quantise Q in the pre-pass even
-                                  at head_dim 128 (q_i8 / q_scale required) */
+#define SAGE_FLAG_PREPASS_Q 8u /* sage_run / sage_run_varlen: INT8 operands from the pre-pass
+                                  (q_i8 / k_i8 required) at either head_dim: exactly
+                                  sage_prepass + sage_attn_fwd */
+#define SAGE_FLAG_CODES16  16u /* sage_prepass only, head_dim 64: q_i8 / k_i8 receive the codes
+                                  as fp16 values (2 bytes each: buffers of twice the size, same
+                                  layouts), for sage_attn_fwd_codes16 */
 
 /* Device-side status bits reported by sage_device_status(). */
 #define SAGE_DEV_TIMEOUT_PRODUCER 0x1
@@ -77,8 +81,11 @@ int sage_abi_version(void);
 const char* sage_last_error(void);
 
 /*
- * Bytes of scratch that sage_per_block_int8 / sage_run need for these sizes (the K-mean
- * and V-absmax partial sums). 0 when neither smoothing nor the FP8 P.V mode is requested.
+ * Bytes of scratch that sage_run needs for these sizes: the K-mean and V-absmax partial sums
+ * (0 when neither smoothing nor the FP8 P.V mode is requested) and, at head_dim 64 unless flags
+ * hold SAGE_FLAG_PREPASS_Q or SAGE_FLAG_FUSED_Q, K's codes as fp16 values (2 bytes per K
+ * element). sage_per_block_int8, sage_prepass and sage_quant_v_fp8 need the partial sums only;
+ * this size serves them too.
  */
 size_t sage_workspace_bytes(int64_t batch, int64_t heads_kv, int64_t seq_kv, int64_t head_dim,
                             int pv_mode, unsigned flags);
@@ -152,6 +159,19 @@ int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
                   int64_t seq_q, int64_t seq_kv, int64_t head_dim, void* stream);
 
 /*
+ * sage_attn_fwd over INT8 codes held as fp16 values (head_dim 64 only; from sage_prepass with
+ * SAGE_FLAG_CODES16): QK^T runs as a kind::f16 MMA, whose fp32 scores equal the INT8 MMA's
+ * (every partial sum is an integer below 2^24), with no int32 -> float step in the softmax.
+ * q_c16 [B, Hq, Sq, 64] and k_c16 [B, Hkv, Skv, 64] contiguous fp16. This is the second half of
+ * sage_run at head_dim 64 (which keeps the Q codes in o and the K codes in its workspace).
+ */
+int sage_attn_fwd_codes16(const void* q_c16, const float* q_scale, const void* k_c16, const float* k_scale,
+                          const void* v, const int64_t v_strides[3], const float* v_scale, void* o,
+                          const int64_t o_strides[3], int dtype, int pv_mode, int causal, int64_t batch,
+                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                          void* stream);
+
+/*
  * sage_attn_fwd with the Q quantisation inside the kernel: each CTA's softmax warps load their
  * 128-row tiles of the caller's 16-bit q ({batch, head, seq} strides q_strides), quantise them
  * exactly as sage_per_block_int8 does (multiplier sm_scale * log2 e, sm_scale <= 0 meaning
@@ -191,7 +211,12 @@ int sage_prepass(const void* q, const void* k, const void* v, int dtype,
  * of at least sage_workspace_bytes(...) bytes. At head_dim 128 (or with SAGE_FLAG_FUSED_Q) Q
  * is quantised inside the attention kernel (sage_prepass with SAGE_FLAG_FUSED_Q, then
  * sage_attn_fwd_fused_q) and q_i8 / q_scale are optional outputs; the result is bit-identical
- * to the pre-pass route (sage_prepass + sage_attn_fwd).
+ * to the pre-pass route (sage_prepass + sage_attn_fwd). At head_dim 64 (unless a flag above
+ * says otherwise) the pre-pass stores the codes as fp16 values, Q's in o itself (each CTA
+ * reads its own query rows before it writes the same rows of o, so o must not overlap k or v)
+ * and K's in the workspace, and QK^T runs on them as a kind::f16 MMA (sage_prepass with
+ * SAGE_FLAG_CODES16 + sage_attn_fwd_codes16): q_i8 / k_i8 are then not used (may be NULL), the
+ * scores are the INT8 MMA's exactly, and the output matches the INT8 route to float rounding.
  */
 int sage_run(const void* q, const void* k, const void* v, void* o, int dtype,
              int64_t batch, int64_t heads_q, int64_t heads_kv,

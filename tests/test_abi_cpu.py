@@ -42,6 +42,12 @@ def test_workspace_bytes():
     assert ws == 2 * 32 * (8192 // 512) * 128 * 8
     ws8 = lib.sage_workspace_bytes(2, 32, 8192, 128, N.SAGE_PV_FP8, N.SAGE_FLAG_SMOOTH_K)
     assert ws8 == ws + 2 * 32 * 16 * 128 * 4
+    # head_dim 64: sage_run's default route also keeps K's fp16 codes in the workspace
+    stats64 = 2 * 32 * 16 * 64 * 8
+    codes64 = 2 * 32 * 8192 * 64 * 2
+    assert lib.sage_workspace_bytes(2, 32, 8192, 64, N.SAGE_PV_16BIT, N.SAGE_FLAG_SMOOTH_K) == stats64 + codes64
+    for route in (N.SAGE_FLAG_PREPASS_Q, N.SAGE_FLAG_FUSED_Q):
+        assert lib.sage_workspace_bytes(2, 32, 8192, 64, N.SAGE_PV_16BIT, N.SAGE_FLAG_SMOOTH_K | route) == stats64
 
 
 def _dummy(n=1 << 12):
@@ -112,7 +118,7 @@ def test_error_message_is_cleared_by_next_call():
     lib = N.load()
     assert _pbi8(head_dim=96) == N.SAGE_ERR_INVALID_ARG
     assert lib.sage_last_error().decode() != ""
-    assert lib.sage_workspace_bytes(1, 1, 1, 64, 0, 0) == 0
+    assert lib.sage_workspace_bytes(1, 1, 1, 128, 0, 0) == 0
     assert _pbi8(strides=(1024, 1024, 100)) == N.SAGE_ERR_INVALID_ARG
     assert "head_dim" not in lib.sage_last_error().decode()
 

@@ -37,9 +37,10 @@ def test_fused_q_output_bit_identical(B, Hq, Hkv, S, Skv, D, dtype, causal, pv):
     q, k, v = _qkv(B, Hq, Hkv, S, D, dtype, seed=S + D, Skv=Skv)
     ref = tb.run(q, k, v, causal=causal, pv=pv, fused_q=False)
     out = tb.run(q, k, v, causal=causal, pv=pv, fused_q=True)
-    auto = tb.run(q, k, v, causal=causal, pv=pv)  # fused at head_dim 128, pre-pass at 64
     assert tb.device_status(DEV) == 0
-    assert torch.equal(out, ref) and torch.equal(auto, ref)
+    assert torch.equal(out, ref)
+    if D == 128:  # sage_run's own choice there is the fused route
+        assert torch.equal(tb.run(q, k, v, causal=causal, pv=pv), ref)
 
 
 @pytest.mark.parametrize("D", [64, 128])

@@ -26,6 +26,7 @@ SAGE_FLAG_SMOOTH_K = 1
 SAGE_FLAG_KM_GIVEN = 2
 SAGE_FLAG_FUSED_Q = 4
 SAGE_FLAG_PREPASS_Q = 8
+SAGE_FLAG_CODES16 = 16
 
 # Every symbol the header declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -46,6 +47,8 @@ SIGNATURES = {
     "sage_quant_v_fp8": (_I, [_P, _I, _I64, _I64, _I64, _I64, _I64P, _P, _P, _P, _SZ, _P]),
     "sage_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I,
                            _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "sage_attn_fwd_codes16": (_I, [_P, _P, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I,
+                                   _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "sage_attn_fwd_fused_q": (_I, [_P, _I64P, _F, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I,
                                    _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "sage_prepass": (_I, [_P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _F, _I, _U,

@@ -133,6 +133,35 @@ struct Varlen {
   int64_t q_tokens, k_tokens;
 };
 
+// INT8 codes held as fp16 values (the head_dim-64 route of sage_run): Q's in a tensor with
+// {batch, head, seq} strides qs, K's in k_i8's layout (contiguous, or [Hkv, tokens, D] packed).
+struct Codes16 {
+  __half* q;
+  const int64_t* qs;
+  __half* k;
+};
+
+// Workspace of the statistics (K column sums, V absmax) and, for sage_run's fp16-code route,
+// of K's fp16 codes after them.
+size_t stats_ws_bytes(int64_t B, int64_t Hkv, int64_t Skv, int64_t D, int pv_mode, unsigned flags) {
+  if (B <= 0 || Hkv <= 0 || Skv <= 0 || D <= 0) return 0;
+  size_t n = 0;
+  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
+  const bool fp8 = pv_mode == SAGE_PV_FP8;
+  if (smooth || fp8) n += align256(ws_ksum_bytes(B, Hkv, Skv, D));
+  if (fp8) n += align256(ws_vmax_bytes(B, Hkv, Skv, D));
+  return n;
+}
+size_t codes_ws_bytes(int64_t B, int64_t Hkv, int64_t Skv, int64_t D) {
+  return align256(static_cast<size_t>(B * Hkv * Skv * D) * sizeof(__half));
+}
+// sage_run's route at head_dim 64: INT8 codes as fp16 values and a kind::f16 QK^T, unless a
+// flag asks for the INT8 operands (SAGE_FLAG_PREPASS_Q) or Q quantised in the kernel
+// (SAGE_FLAG_FUSED_Q, whose codes are INT8).
+bool c16_route(unsigned flags, int64_t head_dim) {
+  return head_dim == 64 && !(flags & (SAGE_FLAG_PREPASS_Q | SAGE_FLAG_FUSED_Q));
+}
+
 int encode_4d(CUtensorMap* map, CUtensorMapDataType dt, int elt_bytes, const void* base, int64_t d0, int64_t d1,
               int64_t d2, int64_t d3, int64_t s1, int64_t s2, int64_t s3, uint32_t box0, uint32_t box1,
               CUtensorMapSwizzle sw) {
@@ -157,11 +186,27 @@ unsigned long long wait_limit_ns() {
 }
 
 // ---------------------------------------------------------------- pre-pass launches
+// The four instantiations: dense or packed sequences, INT8 or (head_dim 64 only) fp16 codes.
+template <int D, typename T>
+void launch_prepass_kernel(const sage::PrepassParams& p, int64_t grid, bool packed, bool c16, cudaStream_t st) {
+  const dim3 g((unsigned)grid);
+  if constexpr (D == 64) {
+    if (c16) {
+      if (packed) sage::prepass_kernel<D, T, true, true><<<g, sage::kQuantThreads, 0, st>>>(p);
+      else sage::prepass_kernel<D, T, false, true><<<g, sage::kQuantThreads, 0, st>>>(p);
+      return;
+    }
+  }
+  if (packed) sage::prepass_kernel<D, T, true><<<g, sage::kQuantThreads, 0, st>>>(p);
+  else sage::prepass_kernel<D, T, false><<<g, sage::kQuantThreads, 0, st>>>(p);
+}
+
 template <int D, typename T>
 int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                    int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs, float q_mult, bool smooth,
                    bool km_given, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean,
-                   uint8_t* v_fp8, float* v_scale, void* ws, const Varlen* vl, cudaStream_t st) {
+                   uint8_t* v_fp8, float* v_scale, void* ws, const Varlen* vl, const Codes16* c16,
+                   cudaStream_t st) {
   const int nchunk = static_cast<int>(cdiv(Skv, sage::kStatsChunk));
   const bool want_v = v_fp8 != nullptr;
   const bool want_km = smooth && !km_given && k != nullptr;
@@ -176,6 +221,11 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
   p.q_mult = q_mult;
   p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
   if (vl) { p.cu_q = vl->cu_q; p.cu_k = vl->cu_k; p.q_tokens = (int)vl->q_tokens; p.k_tokens = (int)vl->k_tokens; }
+  if (c16) {
+    if (D != 64) return fail(SAGE_ERR_INVALID_ARG, "fp16 codes are the head_dim-64 route");
+    p.q_c16 = c16->q; p.k_c16 = c16->k;
+    if (c16->qs) { p.qc_sb = vl ? 0 : c16->qs[0]; p.qc_sh = c16->qs[1]; p.qc_ss = c16->qs[2]; }
+  }
   p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, sage::kVRowsPerCta<D>); p.nchunk = nchunk;
   const int64_t n_q = q ? B * Hq * cdiv(p.nqb, sage::kQBlocksPerCta<D>) : 0;
   const int64_t n_k = k ? B * Hkv * cdiv(p.nkb, sage::kKBlocksPerCta<D>) : 0;
@@ -197,8 +247,7 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
   p.n_v = 0;
   const int64_t grid_a = (int64_t)p.n_q + p.n_stat + p.n_k;
   if (grid_a > 0) {
-    if (vl) sage::prepass_kernel<D, T, true><<<(unsigned)grid_a, sage::kQuantThreads, 0, st>>>(p);
-    else sage::prepass_kernel<D, T, false><<<(unsigned)grid_a, sage::kQuantThreads, 0, st>>>(p);
+    launch_prepass_kernel<D, T>(p, grid_a, vl != nullptr, c16 != nullptr, st);
     SAGE_CUDA_TRY(cudaGetLastError());
   }
   if (need_stats) {
@@ -215,8 +264,7 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
     p.n_v = (int)n_v;
     const int64_t grid_b = (int64_t)p.n_k + p.n_v;
     if (grid_b > 0) {
-      if (vl) sage::prepass_kernel<D, T, true><<<(unsigned)grid_b, sage::kQuantThreads, 0, st>>>(p);
-      else sage::prepass_kernel<D, T, false><<<(unsigned)grid_b, sage::kQuantThreads, 0, st>>>(p);
+      launch_prepass_kernel<D, T>(p, grid_b, vl != nullptr, c16 != nullptr, st);
       SAGE_CUDA_TRY(cudaGetLastError());
     }
   }
@@ -227,28 +275,28 @@ int prepass_dispatch(int dtype, int64_t D, const void* q, const void* k, const v
                      int64_t Hkv, int64_t Sq, int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                      float q_mult, bool smooth, bool km_given, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale,
                      float* k_mean, uint8_t* v_fp8, float* v_scale, void* ws, cudaStream_t st,
-                     const Varlen* vl = nullptr) {
+                     const Varlen* vl = nullptr, const Codes16* c16 = nullptr) {
   if (dtype == SAGE_DTYPE_F16) {
     if (D == 128)
       return launch_prepass<128, __half>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale, k_i8,
-                                         k_scale, k_mean, v_fp8, v_scale, ws, vl, st);
+                                         k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st);
     return launch_prepass<64, __half>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale, k_i8,
-                                      k_scale, k_mean, v_fp8, v_scale, ws, vl, st);
+                                      k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st);
   }
   if (D == 128)
     return launch_prepass<128, __nv_bfloat16>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale,
-                                              k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, st);
+                                              k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st);
   return launch_prepass<64, __nv_bfloat16>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale,
-                                           k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, st);
+                                           k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st);
 }
 
 // ---------------------------------------------------------------- attention launch
-template <int D, int PV, bool OBF16, bool FLASH = false, bool FQ = false>
+template <int D, int PV, bool OBF16, bool FLASH = false, bool FQ = false, bool C16 = false>
 int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const sage::AttnParams& p,
                 cudaStream_t st) {
   constexpr int QT = 2;
-  using C = sage::AttnCfg<D, PV, QT, FLASH>;
-  auto kern = sage::sage_attn_kernel<D, PV, QT, OBF16, FLASH, FQ>;
+  using C = sage::AttnCfg<D, PV, QT, FLASH, C16>;
+  auto kern = sage::sage_attn_kernel<D, PV, QT, OBF16, FLASH, FQ, C16>;
   if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), C::SMEM_BYTES)) return rc;
   dim3 grid((unsigned)p.n_m_ctas, (unsigned)p.Hq, (unsigned)p.B);
   kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, p);
@@ -276,9 +324,16 @@ void set_seq_params(sage::AttnParams& p, const Varlen* vl, const int64_t* os, in
 
 // The INT8 attention instantiations: head_dim x P.V mode x output type, with Q quantised by the
 // pre-pass (FQ = false) or inside the kernel (FQ = true).
-template <bool FQ>
+template <bool FQ, bool C16 = false>
 int attn_dispatch(int64_t D, bool fp8, bool obf, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                   const sage::AttnParams& p, cudaStream_t st) {
+  if constexpr (C16) {  // head_dim 64 only
+    if (D != 64) return fail(SAGE_ERR_INVALID_ARG, "fp16 codes are the head_dim-64 route");
+    if (fp8) return obf ? launch_attn<64, sage::kPvE4M3, true, false, false, true>(tq, tk, tv, p, st)
+                        : launch_attn<64, sage::kPvE4M3, false, false, false, true>(tq, tk, tv, p, st);
+    return obf ? launch_attn<64, sage::kPvBF16, true, false, false, true>(tq, tk, tv, p, st)
+               : launch_attn<64, sage::kPvF16, false, false, false, true>(tq, tk, tv, p, st);
+  }
   if (D == 128) {
     if (fp8) return obf ? launch_attn<128, sage::kPvE4M3, true, false, FQ>(tq, tk, tv, p, st)
                         : launch_attn<128, sage::kPvE4M3, false, false, FQ>(tq, tk, tv, p, st);
@@ -305,16 +360,26 @@ struct FusedQ {
 int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale, const void* v,
               const int64_t* vs, const float* v_scale, void* o, const int64_t* os, int dtype, int pv_mode, int causal,
               int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, cudaStream_t st,
-              const Varlen* vl = nullptr, const FusedQ* fq = nullptr) {
+              const Varlen* vl = nullptr, const FusedQ* fq = nullptr, const Codes16* c16 = nullptr) {
   const bool fp8 = pv_mode == SAGE_PV_FP8;
   // rows of the token axis and batch extent of every tensor map (packed sequences: one batch)
   const int64_t rq = vl ? vl->q_tokens : Sq, rk = vl ? vl->k_tokens : Skv, nb = vl ? 1 : B;
   CUtensorMap tq, tk, tv;
   const CUtensorMapSwizzle swqk = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  if (int rc = encode_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k_i8, D, rk, Hkv, nb, D, rk * D, Hkv * rk * D,
-                         (uint32_t)D, 128, swqk))
-    return rc;
-  if (fq) {
+  if (!c16) {
+    if (int rc = encode_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k_i8, D, rk, Hkv, nb, D, rk * D, Hkv * rk * D,
+                           (uint32_t)D, 128, swqk))
+      return rc;
+  }
+  if (c16) {  // fp16 codes: 128-byte rows at head_dim 64
+    const int64_t* cs = c16->qs;
+    if (int rc = encode_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, c16->q, D, rq, Hq, nb, cs[2], cs[1],
+                           vl ? packed_batch_stride(cs, Hq, rq) : cs[0], (uint32_t)D, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = encode_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, c16->k, D, rk, Hkv, nb, D, rk * D, Hkv * rk * D,
+                           (uint32_t)D, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  } else if (fq) {
     tq = tk;  // not read: the kernel loads Q itself
   } else if (int rc = encode_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q_i8, D, rq, Hq, nb, D, rq * D, Hq * rq * D,
                                 (uint32_t)D, 128, swqk)) {
@@ -341,6 +406,7 @@ int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, cons
     p.q_i8_out = fq->q_i8_out; p.q_scale_out = fq->q_scale_out;
   }
   const bool obf = dtype == SAGE_DTYPE_BF16;
+  if (c16) return attn_dispatch<false, true>(D, fp8, obf, tq, tk, tv, p, st);
   return fq ? attn_dispatch<true>(D, fp8, obf, tq, tk, tv, p, st) : attn_dispatch<false>(D, fp8, obf, tq, tk, tv, p, st);
 }
 
@@ -431,12 +497,8 @@ const char* sage_last_error(void) { return g_last_error.c_str(); }
 size_t sage_workspace_bytes(int64_t batch, int64_t heads_kv, int64_t seq_kv, int64_t head_dim, int pv_mode,
                             unsigned flags) {
   if (batch <= 0 || heads_kv <= 0 || seq_kv <= 0 || head_dim <= 0) return 0;
-  size_t n = 0;
-  const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
-  const bool fp8 = pv_mode == SAGE_PV_FP8;
-  if (smooth || fp8) n += align256(ws_ksum_bytes(batch, heads_kv, seq_kv, head_dim));
-  if (fp8) n += align256(ws_vmax_bytes(batch, heads_kv, seq_kv, head_dim));
-  return n;
+  return stats_ws_bytes(batch, heads_kv, seq_kv, head_dim, pv_mode, flags) +
+         (c16_route(flags, head_dim) ? codes_ws_bytes(batch, heads_kv, seq_kv, head_dim) : 0);
 }
 
 int sage_per_block_int8(const void* q, const void* k, int dtype, int64_t batch, int64_t heads_q, int64_t heads_kv,
@@ -454,7 +516,7 @@ int sage_per_block_int8(const void* q, const void* k, int dtype, int64_t batch, 
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
   if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
   const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
-  const size_t need = km_given ? 0 : sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_16BIT, flags);
+  const size_t need = km_given ? 0 : stats_ws_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_16BIT, flags);
   if (need && (!workspace || workspace_bytes < need))
     return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   if (int rc = check_arch()) return rc;
@@ -478,7 +540,7 @@ int sage_per_block_int8_noalloc(const void* q, const void* k, int dtype, int64_t
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
   if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
   const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
-  const size_t need = km_given ? 0 : sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_16BIT, flags);
+  const size_t need = km_given ? 0 : stats_ws_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_16BIT, flags);
   if (need > kNoAllocScratchBytes)
     return fail(SAGE_ERR_INVALID_ARG,
                 "sizes need %zu bytes of statistics scratch; the built-in scratch of "
@@ -502,7 +564,7 @@ int sage_quant_v_fp8(const void* v, int dtype, int64_t batch, int64_t heads_kv, 
   if (int rc = check_strides("v", v_strides)) return rc;
   if (!v || !v_fp8 || !v_scale) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(v) || !aligned16(v_fp8)) return fail(SAGE_ERR_INVALID_ARG, "v/v_fp8 must be 16-byte aligned");
-  const size_t need = sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_FP8, 0);
+  const size_t need = stats_ws_bytes(batch, heads_kv, seq_kv, head_dim, SAGE_PV_FP8, 0);
   if (!workspace || workspace_bytes < need)
     return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   if (int rc = check_arch()) return rc;
@@ -565,6 +627,37 @@ int sage_attn_fwd_fused_q(const void* q, const int64_t q_strides[3], float sm_sc
                    batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream), nullptr, &fq);
 }
 
+int sage_attn_fwd_codes16(const void* q_c16, const float* q_scale, const void* k_c16, const float* k_scale,
+                          const void* v, const int64_t v_strides[3], const float* v_scale, void* o,
+                          const int64_t o_strides[3], int dtype, int pv_mode, int causal, int64_t batch,
+                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                          void* stream) {
+  g_last_error.clear();
+  if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  if (head_dim != 64) return fail(SAGE_ERR_INVALID_ARG, "fp16 codes are the head_dim-64 route");
+  if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
+    return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
+  if (causal && seq_q != seq_kv)
+    return fail(SAGE_ERR_INVALID_ARG, "causal attention needs seq_q == seq_kv (got %lld, %lld)", (long long)seq_q,
+                (long long)seq_kv);
+  if (int rc = check_strides("o", o_strides)) return rc;
+  if (pv_mode == SAGE_PV_16BIT) {
+    if (int rc = check_strides("v", v_strides)) return rc;
+  } else if (!v_scale) {
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs v_scale");
+  }
+  if (!q_c16 || !q_scale || !k_c16 || !k_scale || !v || !o) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(q_c16) || !aligned16(k_c16) || !aligned16(v) || !aligned16(o))
+    return fail(SAGE_ERR_INVALID_ARG, "q_c16/k_c16/v/o must be 16-byte aligned");
+  if (int rc = check_arch()) return rc;
+  const int64_t qcs[3] = {heads_q * seq_q * head_dim, seq_q * head_dim, head_dim};
+  const Codes16 c16{static_cast<__half*>(const_cast<void*>(q_c16)), qcs,
+                    static_cast<__half*>(const_cast<void*>(k_c16))};
+  return attn_impl(nullptr, q_scale, nullptr, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal,
+                   batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream), nullptr,
+                   nullptr, &c16);
+}
+
 namespace {
 // Where sage_run / sage_run_varlen quantise Q: inside the attention kernel at head_dim 128
 // (H8K 1.817 -> 1.774 ms per call: the pre-pass no longer reads Q and writes its INT8 copy) or
@@ -575,13 +668,20 @@ bool fused_q_for(unsigned flags, int64_t head_dim) {
   return (flags & SAGE_FLAG_FUSED_Q) != 0 || head_dim == 128;
 }
 
+// The three ways sage_run can feed the attention kernel.
+enum class Route { kInt8, kFusedQ, kCodes16 };
+Route run_route(unsigned flags, int64_t head_dim) {
+  if (fused_q_for(flags, head_dim)) return Route::kFusedQ;
+  return c16_route(flags, head_dim) ? Route::kCodes16 : Route::kInt8;
+}
+
 // Shared validation of sage_prepass / sage_run; returns SAGE_OK or the failing status.
 int check_run_args(const void* q, const void* k, const void* v, int dtype, int64_t batch, int64_t heads_q,
                    int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim, const int64_t* q_strides,
                    const int64_t* k_strides, const int64_t* v_strides, int pv_mode, unsigned flags,
                    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale,
                    const float* k_mean, const uint8_t* v_fp8, const float* v_scale, const void* workspace,
-                   size_t workspace_bytes, bool fused_q) {
+                   size_t workspace_bytes, Route route, bool run) {
   if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
   if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
@@ -590,10 +690,12 @@ int check_run_args(const void* q, const void* k, const void* v, int dtype, int64
   if (int rc = check_strides("q", q_strides)) return rc;
   if (int rc = check_strides("k", k_strides)) return rc;
   if (int rc = check_strides("v", v_strides)) return rc;
-  // where Q is quantised in the attention kernel its codes / scales are optional outputs
-  if (!q || !k || !v || !k_i8 || !k_scale || (!fused_q && (!q_i8 || !q_scale)) || (!q_i8 != !q_scale))
+  // Q quantised in the attention kernel: its codes / scales are optional outputs; sage_run's
+  // fp16-code route keeps the codes in o and the workspace: q_i8 / k_i8 are not used
+  if (!q || !k || !v || !k_scale || (route != Route::kCodes16 && !k_i8) || (route == Route::kCodes16 && !q_scale) ||
+      (route == Route::kInt8 && (!q_i8 || !q_scale)) || (route == Route::kFusedQ && !q_i8 != !q_scale))
     return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (q_i8 && !aligned16(q_i8)) || !aligned16(k_i8))
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (q_i8 && !aligned16(q_i8)) || (k_i8 && !aligned16(k_i8)))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/v/q_i8/k_i8 must be 16-byte aligned");
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
   const bool fp8 = pv_mode == SAGE_PV_FP8;
@@ -601,8 +703,8 @@ int check_run_args(const void* q, const void* k, const void* v, int dtype, int64
   if (fp8 && (!v_fp8 || !v_scale || !aligned16(v_fp8)))
     return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs 16-byte aligned v_fp8 and v_scale");
   const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
-  const size_t need =
-      sage_workspace_bytes(batch, heads_kv, seq_kv, head_dim, pv_mode, km_given ? 0u : flags);
+  const size_t need = stats_ws_bytes(batch, heads_kv, seq_kv, head_dim, pv_mode, km_given ? 0u : flags) +
+                      ((run && route == Route::kCodes16) ? codes_ws_bytes(batch, heads_kv, seq_kv, head_dim) : 0);
   if (need && (!workspace || workspace_bytes < need))
     return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   return SAGE_OK;
@@ -615,19 +717,25 @@ int sage_prepass(const void* q, const void* k, const void* v, int dtype, int64_t
                  unsigned flags, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean,
                  uint8_t* v_fp8, float* v_scale, void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error.clear();
+  const bool fused_q = (flags & SAGE_FLAG_FUSED_Q) != 0;  // Q is left to sage_attn_fwd_fused_q
+  const bool codes16 = (flags & SAGE_FLAG_CODES16) != 0;  // codes as fp16 values, for sage_attn_fwd_codes16
+  if (codes16 && (fused_q || head_dim != 64))
+    return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_CODES16 is the head_dim-64 route and needs Q from the pre-pass");
   if (int rc = check_run_args(q, k, v, dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, q_strides,
                               k_strides, v_strides, pv_mode, flags, q_i8, q_scale, k_i8, k_scale, k_mean, v_fp8,
-                              v_scale, workspace, workspace_bytes, (flags & SAGE_FLAG_FUSED_Q) != 0))
+                              v_scale, workspace, workspace_bytes, fused_q ? Route::kFusedQ : Route::kInt8, false))
     return rc;
   if (int rc = check_arch()) return rc;
   const bool fp8 = pv_mode == SAGE_PV_FP8;
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
-  const bool fused_q = (flags & SAGE_FLAG_FUSED_Q) != 0;  // Q is left to sage_attn_fwd_fused_q
+  const int64_t qcs[3] = {heads_q * seq_q * head_dim, seq_q * head_dim, head_dim};  // contiguous Q codes
+  const Codes16 c16{reinterpret_cast<__half*>(q_i8), qcs, reinterpret_cast<__half*>(k_i8)};
   return prepass_dispatch(dtype, head_dim, fused_q ? nullptr : q, k, fp8 ? v : nullptr, batch, heads_q, heads_kv,
                           seq_q, seq_kv, q_strides, k_strides, v_strides, q_multiplier(sm_scale, head_dim), smooth,
                           smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, fused_q ? nullptr : q_i8,
                           fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr,
-                          fp8 ? v_scale : nullptr, workspace, static_cast<cudaStream_t>(stream));
+                          fp8 ? v_scale : nullptr, workspace, static_cast<cudaStream_t>(stream), nullptr,
+                          codes16 ? &c16 : nullptr);
 }
 
 int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch, int64_t heads_q,
@@ -637,9 +745,10 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
              float* k_scale, float* k_mean, uint8_t* v_fp8, float* v_scale, void* workspace,
              size_t workspace_bytes, void* stream) {
   g_last_error.clear();
+  const Route route = run_route(flags, head_dim);
   if (int rc = check_run_args(q, k, v, dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, q_strides,
                               k_strides, v_strides, pv_mode, flags, q_i8, q_scale, k_i8, k_scale, k_mean, v_fp8,
-                              v_scale, workspace, workspace_bytes, fused_q_for(flags, head_dim)))
+                              v_scale, workspace, workspace_bytes, route, true))
     return rc;
   if (causal && seq_q != seq_kv)
     return fail(SAGE_ERR_INVALID_ARG, "causal attention needs seq_q == seq_kv (got %lld, %lld)", (long long)seq_q,
@@ -650,20 +759,28 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool fp8 = pv_mode == SAGE_PV_FP8;
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
-  // Q quantised by the attention kernel itself (the pre-pass then handles K and V only) at
-  // head_dim 128 or with SAGE_FLAG_FUSED_Q; the codes and output are identical either way
-  const bool fused_q = fused_q_for(flags, head_dim);
+  // head_dim 128 (or SAGE_FLAG_FUSED_Q): Q quantised by the attention kernel itself, the pre-pass
+  // handles K (and V). head_dim 64: the pre-pass stores the codes as fp16 values, Q's in o (each
+  // CTA reads its own query rows before it writes the same rows of o) and K's in the workspace
+  // after the statistics, for the kernel's kind::f16 QK^T. SAGE_FLAG_PREPASS_Q: INT8 operands.
+  const bool fused_q = route == Route::kFusedQ;
+  const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
   const float q_mult = q_multiplier(sm_scale, head_dim);
+  Codes16 c16{};
+  if (route == Route::kCodes16) {
+    const size_t off = stats_ws_bytes(batch, heads_kv, seq_kv, head_dim, pv_mode, km_given ? 0u : flags);
+    c16 = Codes16{static_cast<__half*>(o), o_strides, reinterpret_cast<__half*>(static_cast<char*>(workspace) + off)};
+  }
+  const Codes16* cp = route == Route::kCodes16 ? &c16 : nullptr;
   if (int rc = prepass_dispatch(dtype, head_dim, fused_q ? nullptr : q, k, fp8 ? v : nullptr, batch, heads_q,
-                                heads_kv, seq_q, seq_kv, q_strides, k_strides, v_strides, q_mult, smooth,
-                                smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, fused_q ? nullptr : q_i8,
-                                fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr,
-                                fp8 ? v_scale : nullptr, workspace, st))
+                                heads_kv, seq_q, seq_kv, q_strides, k_strides, v_strides, q_mult, smooth, km_given,
+                                fused_q ? nullptr : q_i8, fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean,
+                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st, nullptr, cp))
     return rc;
   const FusedQ fq{q, q_strides, q_mult, q_i8, q_scale};
   return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, v_strides,
                    fp8 ? v_scale : nullptr, o, o_strides, dtype, pv_mode, causal, batch, heads_q, heads_kv, seq_q,
-                   seq_kv, head_dim, st, nullptr, fused_q ? &fq : nullptr);
+                   seq_kv, head_dim, st, nullptr, fused_q ? &fq : nullptr, cp);
 }
 
 int sage_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,
@@ -735,7 +852,7 @@ int sage_per_block_int8_varlen(const void* q, const void* k, int dtype, int64_t 
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
   if (smooth && !k_mean) return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_SMOOTH_K needs k_mean");
   const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
-  const size_t need = km_given ? 0 : sage_workspace_bytes(batch, heads_kv, max_seq_kv, head_dim, SAGE_PV_16BIT, flags);
+  const size_t need = km_given ? 0 : stats_ws_bytes(batch, heads_kv, max_seq_kv, head_dim, SAGE_PV_16BIT, flags);
   if (need && (!workspace || workspace_bytes < need))
     return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   if (int rc = check_arch()) return rc;
@@ -765,11 +882,14 @@ int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dt
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
   if ((flags & SAGE_FLAG_FUSED_Q) && (flags & SAGE_FLAG_PREPASS_Q))
     return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_FUSED_Q and SAGE_FLAG_PREPASS_Q exclude each other");
-  const bool fused_q = fused_q_for(flags, head_dim);
-  if (!q || !k || !v || !o || !k_i8 || !k_scale || (!fused_q && (!q_i8 || !q_scale)) || (!q_i8 != !q_scale))
+  const Route route = run_route(flags, head_dim);
+  const bool fused_q = route == Route::kFusedQ;
+  if (!q || !k || !v || !o || !k_scale || (route != Route::kCodes16 && !k_i8) ||
+      (route == Route::kCodes16 && !q_scale) || (route == Route::kInt8 && (!q_i8 || !q_scale)) ||
+      (fused_q && !q_i8 != !q_scale))
     return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (q_i8 && !aligned16(q_i8)) ||
-      !aligned16(k_i8))
+      (k_i8 && !aligned16(k_i8)))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o/q_i8/k_i8 must be 16-byte aligned");
   const bool smooth = (flags & SAGE_FLAG_SMOOTH_K) != 0;
   const bool fp8 = pv_mode == SAGE_PV_FP8;
@@ -777,22 +897,26 @@ int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dt
   if (fp8 && (!v_fp8 || !v_scale || !aligned16(v_fp8)))
     return fail(SAGE_ERR_INVALID_ARG, "SAGE_PV_FP8 needs 16-byte aligned v_fp8 and v_scale");
   const bool km_given = smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0;
-  const size_t need = sage_workspace_bytes(batch, heads_kv, max_seq_kv, head_dim, pv_mode, km_given ? 0u : flags);
+  const size_t stats = stats_ws_bytes(batch, heads_kv, max_seq_kv, head_dim, pv_mode, km_given ? 0u : flags);
+  // batch * max_seq_kv >= total_kv: the codes' region also holds the packed [Hkv, total_kv, D] codes
+  const size_t need = stats + (route == Route::kCodes16 ? codes_ws_bytes(batch, heads_kv, max_seq_kv, head_dim) : 0);
   if (need && (!workspace || workspace_bytes < need))
     return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   if (int rc = check_arch()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Varlen vl{cu_seqlens_q, cu_seqlens_kv, total_q, total_kv};
   const float q_mult = q_multiplier(sm_scale, head_dim);
+  const Codes16 c16{static_cast<__half*>(o), os, reinterpret_cast<__half*>(static_cast<char*>(workspace) + stats)};
+  const Codes16* cp = route == Route::kCodes16 ? &c16 : nullptr;
   if (int rc = prepass_dispatch(dtype, head_dim, fused_q ? nullptr : q, k, fp8 ? v : nullptr, batch, heads_q,
                                 heads_kv, max_seq_q, max_seq_kv, qs, ks, vs, q_mult, smooth, km_given,
                                 fused_q ? nullptr : q_i8, fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean,
-                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st, &vl))
+                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st, &vl, cp))
     return rc;
   const FusedQ fq{q, qs, q_mult, q_i8, q_scale};
   return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, vs,
                    fp8 ? v_scale : nullptr, o, os, dtype, pv_mode, causal, batch, heads_q, heads_kv, max_seq_q,
-                   max_seq_kv, head_dim, st, &vl, fused_q ? &fq : nullptr);
+                   max_seq_kv, head_dim, st, &vl, fused_q ? &fq : nullptr, cp);
 }
 
 int sage_flash_attn_varlen_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,

@@ -69,13 +69,19 @@ struct AttnParams {
   float* q_scale_out;
 };
 
-template <int D, int PV, int QT, bool FLASH = false>
+// C16: the INT8 codes of Q and K arrive as fp16 values (exact: |code| <= 127) and QK^T runs as a
+// kind::f16 MMA into fp32 scores. Each product is an integer below 2^14 and each row sum one
+// below 2^21 (D <= 128), so every partial sum is exact in fp32 and the scores equal the INT8
+// MMA's to the bit, as floats, with no int32 -> float step in the softmax.
+template <int D, int PV, int QT, bool FLASH = false, bool C16 = false>
 struct AttnCfg {
   static_assert(!FLASH || PV != kPvE4M3, "the flash variant keeps P in the input dtype");
+  static_assert(!(FLASH && C16), "C16 is the INT8 path's operand form");
+  static constexpr bool QK_F16 = FLASH || C16;  // Q/K tiles hold 16-bit values, QK^T is kind::f16
   static constexpr int BM = 128;               // query rows per tile
   static constexpr int BN = 128;               // keys per tile
   static constexpr int V_ELT = (PV == kPvE4M3) ? 1 : 2;
-  static constexpr int QK_ELT = FLASH ? 2 : 1; // bytes per Q/K element (int8, or fp16/bf16)
+  static constexpr int QK_ELT = QK_F16 ? 2 : 1; // bytes per Q/K element (int8, or fp16/bf16)
   // K/V ring stages (shared memory: QT Q tiles + NS x (K + V) tiles within 227 KB)
   static constexpr int NS = FLASH ? ((D == 128) ? 2 : 4) : ((D == 128) ? ((PV == kPvE4M3) ? 4 : 3) : 4);
   static constexpr int Q_TILE = BM * D * QK_ELT;  // bytes
@@ -88,7 +94,7 @@ struct AttnCfg {
   // The copy shape follows the measurements: with 16-bit P.V, whose MMAs keep the tensor pipe
   // busier, the broadcasting 32x128b.warpx4 copy (s8k_d64 1.618 -> 1.587 ms; 128x256b made it
   // slower); with FP8 P.V the 128x256b copy (C4 1.807 -> 1.772 ms).
-  static constexpr bool PRE_BIAS = (D == 64) && !FLASH;
+  static constexpr bool PRE_BIAS = (D == 64) && !QK_F16;
   static constexpr int OFF_BIAS = OFF_V + NS * V_TILE;          // 4 KB of 0x4B400000 words
   static constexpr int OFF_BAR = OFF_BIAS + (PRE_BIAS ? 4096 : 0);
   // q, kfull/vfull/kvempty per stage, sfull/phalf/pfull/odone/sload/pvdone per query tile
@@ -135,6 +141,7 @@ struct AttnCfg {
   static constexpr bool PV_FP8 = (PV == kPvE4M3);
   static constexpr uint32_t PV_FMT = (PV == kPvBF16) ? kFmtBF16 : ((PV == kPvE4M3) ? kFmtE4M3 : kFmtF16);
   static constexpr uint32_t IDESC_QK = FLASH ? make_idesc(kFmtD_F32, PV_FMT, PV_FMT, 0, 0, BM, BN)
+                                     : C16   ? make_idesc(kFmtD_F32, kFmtF16, kFmtF16, 0, 0, BM, BN)
                                              : make_idesc(kFmtD_S32, kFmtS8, kFmtS8, 0, 0, BM, BN);
   static constexpr uint32_t IDESC_PV = make_idesc(kFmtD_F32, PV_FMT, PV_FMT, 0, 1, BM, D);
   // Softmax: the running max is only raised when a tile's max exceeds it by more than LAZY
@@ -158,7 +165,7 @@ enum : int { kDevTimeoutProducer = 1, kDevTimeoutMma = 2, kDevTimeoutSoftmax = 4
 // the S columns are first filled with the word 0x4B400000 (tcgen05.cp from a constant block) and
 // the MMA accumulates onto it, so each int32 score s arrives as the bit pattern of the float
 // 1.5 * 2^23 + s (|s| <= 127^2 * 64 < 2^22), which softmax uses without an integer add.
-template <class C, bool FLASH>
+template <class C>
 __device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint32_t k_tile, uint32_t bias_addr) {
   if constexpr (C::PRE_BIAS) {
     const uint64_t bd = make_smem_desc(bias_addr, 128, 256, 0);  // any layout: every word is equal
@@ -174,7 +181,7 @@ __device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint3
   for (int kk = 0; kk < C::QK_STEPS; ++kk) {
     const uint64_t qd = make_smem_desc(q_tile + C::qk_step_offset(kk, C::BM), 16, C::QK_SBO, C::QK_LAYOUT);
     const uint64_t kd = make_smem_desc(k_tile + C::qk_step_offset(kk, C::BN), 16, C::QK_SBO, C::QK_LAYOUT);
-    if constexpr (FLASH)
+    if constexpr (C::QK_F16)
       umma_f16_ss(s_tmem, qd, kd, C::IDESC_QK, kk > 0);
     else
       umma_i8_ss(s_tmem, qd, kd, C::IDESC_QK, (kk > 0 || C::PRE_BIAS) ? 1u : 0u);
@@ -247,11 +254,12 @@ __device__ __forceinline__ float fused_q_tile(const AttnParams& p, uint8_t* qtil
 
 // FQ: Q arrives as the caller's 16-bit tensor and is quantised by the softmax warps
 // (fused_q_tile); a separate instantiation, so the default kernel carries none of that code.
-template <int D, int PV, int QT, bool OBF16, bool FLASH, bool FQ = false>
-__global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
+template <int D, int PV, int QT, bool OBF16, bool FLASH, bool FQ = false, bool C16 = false>
+__global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH, C16>::NUM_THREADS, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  using C = AttnCfg<D, PV, QT, FLASH>;
+  using C = AttnCfg<D, PV, QT, FLASH, C16>;
+  static_assert(!(FQ && C16), "Q quantised in the kernel is stored as INT8 codes");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -384,7 +392,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
           if (nkv[t] == 0) continue;
-          issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr, bias_addr);
+          issue_qk<C>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr, bias_addr);
           umma_commit(bar_sfull + t);
         }
       }
@@ -405,7 +413,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
             }
             SAGE_T_MARK(3)
             tc_fence_after();
-            issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE, bias_addr);
+            issue_qk<C>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE, bias_addr);
             umma_commit(bar_sfull + t);
           }
           if (!ok) break;
@@ -450,7 +458,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
               knext_ready = true;
               tc_fence_after();
             }
-            issue_qk<C, FLASH>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE, bias_addr);
+            issue_qk<C>(tmem_base + 256 * t, q_addr + t * C::Q_TILE, k_addr + s1 * C::K_TILE, bias_addr);
             umma_commit(bar_sfull + t);
           }
         }
@@ -496,8 +504,8 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
     bool ok = true;
     SAGE_T_DECL
     // INT8 scores are biased: 1.5 * 2^23 has bit pattern 0x4B400000, and 0x4B400000 + s is the
-    // float 1.5 * 2^23 + s for |s| < 2^22. fp32 scores (FLASH) are used as they are.
-    constexpr float kMagic = FLASH ? 0.0f : 12582912.0f;
+    // float 1.5 * 2^23 + s for |s| < 2^22. fp32 scores (FLASH, C16) are used as they are.
+    constexpr float kMagic = C::QK_F16 ? 0.0f : 12582912.0f;
     // D = 128: the two K block scales of tile j+1 are loaded during iteration j, so the loads
     // are in flight while tile j+1's scores are computed (H8K 1.681 -> 1.655 ms). At D = 64 the
     // same change made s8k_d64 4 % slower, so there they are loaded where they are used.
@@ -532,7 +540,7 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH>::NUM_THREADS, 1)
         // int32 score s -> float 12582912 + s exactly (an integer add instead of a conversion);
         // monotone in s, so maxima can be taken on these biased values.
 #pragma unroll
-        for (int c = 0; c < 128; ++c) b[c] = __uint_as_float((FLASH || C::PRE_BIAS) ? sr[c] : sr[c] + 0x4B400000u);
+        for (int c = 0; c < 128; ++c) b[c] = __uint_as_float((C::QK_F16 || C::PRE_BIAS) ? sr[c] : sr[c] + 0x4B400000u);
       }
       SAGE_T_MARK(1)
       const int key0 = j * C::BN;

@@ -128,6 +128,14 @@ __device__ __forceinline__ void quant_two(float2 x, float2 s, float2 ns, float2 
   b = __float2int_rz(z.y);
 }
 
+// Two INT8 codes (as integers in [-127, 127]) as an fp16 pair: c + 25728 is the bit pattern of
+// the fp16 value c + 1152 (exponent 10: ulp 1 in [1024, 2048)), and subtracting 1152 is exact.
+__device__ __forceinline__ uint32_t codes_to_half2(int a, int b) {
+  const uint32_t bits = __byte_perm(static_cast<uint32_t>(a + 25728), static_cast<uint32_t>(b + 25728), 0x5410);
+  const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&bits), __float2half2_rn(1152.0f));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // Low bytes of four integers packed little-endian into one word (three byte permutes).
 __device__ __forceinline__ uint32_t pack4_lo_bytes(int a, int b, int c, int d) {
   const uint32_t ab = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
@@ -158,6 +166,12 @@ struct PrepassParams {
   const int* cu_q;
   const int* cu_k;
   int q_tokens, k_tokens;
+  // fp16 codes (C16 instantiations): the same INT8 codes as fp16 values, for the attention
+  // kernel's kind::f16 QK^T. Q's go to q_c16 with element strides qc_sb/qc_sh/qc_ss (batch,
+  // head, token), K's to k_c16 in k_i8's layout.
+  __half* q_c16;
+  int64_t qc_sb, qc_sh, qc_ss;
+  __half* k_c16;
   // CTA roles of this launch, in grid order: Q blocks, statistics chunks, K blocks, V blocks
   int n_q, n_stat, n_k, n_v;
   int stat_k, stat_v;   // which statistics the statistics CTAs gather
@@ -165,7 +179,7 @@ struct PrepassParams {
 
 // ---------------------------------------------------------------- roles
 // NSUB consecutive scale blocks of BLK rows, all rows loaded up front.
-template <int D, typename T, int BLK, int NSUB, bool PACKED>
+template <int D, typename T, int BLK, int NSUB, bool PACKED, bool C16>
 __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta, bool isq, float* red) {
   constexpr int TPR = D / 8;                 // threads per row (8 channels each)
   constexpr int RPP = kQuantThreads / TPR;   // rows per pass
@@ -241,6 +255,17 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
     if (threadIdx.x == b && grp * NSUB + b < nb) (isq ? p.q_scale : p.k_scale)[head * nb + grp * NSUB + b] = scale[b];
   const size_t first_row = PACKED ? (size_t)hh * (isq ? p.q_tokens : p.k_tokens) + sp.base : head * (size_t)S;
   int8_t* dst = (isq ? p.q_i8 : p.k_i8) + first_row * D + g * 8;
+  // C16: Q codes at q_c16 (its own strides), K codes at k_c16 (k_i8's layout, 2 bytes each)
+  __half* dst16 = nullptr;
+  int64_t ss16 = D;
+  if constexpr (C16) {
+    if (isq) {
+      dst16 = p.q_c16 + (int64_t)sp.batch * p.qc_sb + (int64_t)hh * p.qc_sh + (int64_t)sp.base * p.qc_ss + g * 8;
+      ss16 = p.qc_ss;
+    } else {
+      dst16 = p.k_c16 + first_row * D + g * 8;
+    }
+  }
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const int row = row0 + r + i * RPP;
@@ -257,8 +282,14 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
         if (isq) x = fmul2(x, mult2);
         quant_two(x, s2, ns2, r2, qv[e], qv[e + 1]);
       }
-      *reinterpret_cast<uint2*>(dst + (size_t)row * D) =
-          make_uint2(pack4_lo_bytes(qv[0], qv[1], qv[2], qv[3]), pack4_lo_bytes(qv[4], qv[5], qv[6], qv[7]));
+      if constexpr (C16) {
+        *reinterpret_cast<uint4*>(dst16 + (int64_t)row * ss16) =
+            make_uint4(codes_to_half2(qv[0], qv[1]), codes_to_half2(qv[2], qv[3]), codes_to_half2(qv[4], qv[5]),
+                       codes_to_half2(qv[6], qv[7]));
+      } else {
+        *reinterpret_cast<uint2*>(dst + (size_t)row * D) =
+            make_uint2(pack4_lo_bytes(qv[0], qv[1], qv[2], qv[3]), pack4_lo_bytes(qv[4], qv[5], qv[6], qv[7]));
+      }
     }
   }
 }
@@ -386,21 +417,22 @@ __device__ __forceinline__ void vquant_role(const PrepassParams& p, int cta) {
 
 // One launch of the pre-pass: CTA roles in grid order Q blocks | statistics chunks | K blocks | V blocks.
 // PACKED: variable-length batches (p.cu_q / p.cu_k set); a separate instantiation keeps the
-// dense path's code and registers as they are without the sequence offsets.
-template <int D, typename T, bool PACKED>
+// dense path's code and registers as they are without the sequence offsets. C16: codes stored as
+// fp16 values (q_c16 / k_c16) instead of INT8 bytes.
+template <int D, typename T, bool PACKED, bool C16 = false>
 __global__ void __launch_bounds__(kQuantThreads) prepass_kernel(PrepassParams p) {
   constexpr int RPP = kQuantThreads / (D / 8);
   __shared__ double sum_red[RPP][D];
   __shared__ float max_red[RPP][D];
   __shared__ float red[4 * (kQuantThreads / 32)];
   int cta = blockIdx.x;
-  if (cta < p.n_q) { quant_block_role<D, T, 128, kQBlocksPerCta<D>, PACKED>(p, cta, true, red); return; }
+  if (cta < p.n_q) { quant_block_role<D, T, 128, kQBlocksPerCta<D>, PACKED, C16>(p, cta, true, red); return; }
   cta -= p.n_q;
   if (cta < p.n_stat) { stats_role<D, T, PACKED>(p, cta, sum_red, max_red); return; }
   cta -= p.n_stat;
   // K and V blocks run in reverse head order: the statistics CTAs of the previous launch read
   // the last heads most recently, so their rows are the ones still in L2
-  if (cta < p.n_k) { quant_block_role<D, T, 64, kKBlocksPerCta<D>, PACKED>(p, p.n_k - 1 - cta, false, red); return; }
+  if (cta < p.n_k) { quant_block_role<D, T, 64, kKBlocksPerCta<D>, PACKED, C16>(p, p.n_k - 1 - cta, false, red); return; }
   cta -= p.n_k;
   vquant_role<D, T, PACKED>(p, p.n_v - 1 - cta);
 }

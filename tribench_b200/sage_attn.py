@@ -180,10 +180,14 @@ class SagePlan:
     """Preallocated intermediates for repeated calls on one shape (no per-call allocation).
 
     ``plan.run(q, k, v, o)`` is one ``sage_run`` C call: pre-pass kernels + attention kernel.
-    ``fused_q``: where Q is quantised — True: inside the attention kernel (the pre-pass handles
-    K and V only; no INT8 Q buffer unless ``keep_q_int8``), False: in the pre-pass, None: as
-    sage_run chooses (inside the kernel at head_dim 128, the faster route there; in the pre-pass
-    at 64). Codes and output are bit-identical either way.
+    ``fused_q`` picks how the attention kernel gets its operands (``self.route``):
+      * None (sage_run's choice): at head_dim 128 "fused" — Q quantised inside the attention
+        kernel, the pre-pass handles K and V; at 64 "codes16" — the pre-pass stores the codes
+        as fp16 values and QK^T runs as a kind::f16 MMA on them (same scores, no int32 -> float
+        step; the Q codes live in the output buffer until the kernel overwrites them);
+      * True: "fused" at either head_dim (no INT8 Q buffer unless ``keep_q_int8``);
+      * False: "int8" — INT8 operands from the pre-pass (sage_prepass + sage_attn_fwd).
+    "fused" and "int8" give bit-identical output; "codes16" matches them to float rounding.
     """
 
     def __init__(self, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, dtype, device, *, pv="16bit",
@@ -194,64 +198,93 @@ class SagePlan:
         self.dtype, self.device = dtype, torch.device(device)
         self.pv_mode = _PV[pv]
         self.flags = N.SAGE_FLAG_SMOOTH_K if smooth_k else 0
-        self.fused_q = (head_dim == 128) if fused_q is None else bool(fused_q)
+        if fused_q is None:
+            self.route = "fused" if head_dim == 128 else "codes16"
+        else:
+            self.route = "fused" if fused_q else "int8"
+        self.fused_q = self.route == "fused"
+        self.route_flag = {"fused": N.SAGE_FLAG_FUSED_Q, "int8": N.SAGE_FLAG_PREPASS_Q, "codes16": 0}[self.route]
         self.causal, self.sm_scale = bool(causal), sm_scale
         B, Hq, Hkv, Sq, Skv, D = self.shape
         dev = self.device
-        want_q = not self.fused_q or keep_q_int8
+        want_q = self.route == "int8" or (self.fused_q and keep_q_int8)
+        want_k = self.route != "codes16"
         self.quant = SageQuant(
             q_int8=torch.empty((B, Hq, Sq, D), dtype=torch.int8, device=dev) if want_q else None,
-            q_scale=torch.empty((B, Hq, (Sq + 127) // 128), dtype=torch.float32, device=dev) if want_q else None,
-            k_int8=torch.empty((B, Hkv, Skv, D), dtype=torch.int8, device=dev),
+            q_scale=torch.empty((B, Hq, (Sq + 127) // 128), dtype=torch.float32, device=dev)
+            if (want_q or self.route == "codes16") else None,
+            k_int8=torch.empty((B, Hkv, Skv, D), dtype=torch.int8, device=dev) if want_k else None,
             k_scale=torch.empty((B, Hkv, (Skv + 63) // 64), dtype=torch.float32, device=dev),
             k_mean=torch.empty((B, Hkv, D), dtype=torch.float32, device=dev) if smooth_k else None,
             v_fp8=torch.empty((B, Hkv, Skv, D), dtype=torch.uint8, device=dev) if self.pv_mode else None,
             v_scale=torch.empty((B, Hkv, D), dtype=torch.float32, device=dev) if self.pv_mode else None,
         )
-        self.ws_bytes = workspace_bytes(B, Hkv, Skv, D, pv, smooth_k)
+        self.codes16 = None  # (q, k) fp16 code buffers of the split form, allocated by prepass()
+        self.ws_bytes = int(N.load().sage_workspace_bytes(B, Hkv, Skv, D, self.pv_mode, self.flags | self.route_flag))
         self.ws = torch.empty(max(self.ws_bytes, 1), dtype=torch.uint8, device=dev)
 
+    def _sm_scale(self):
+        return ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale))
+
     def prepass(self, q, k, v, tensor_layout="HND"):
-        """The pre-pass half of run() (sage_prepass): fills self.quant from k (and v for FP8), and
-        from q unless the plan quantises Q in the attention kernel."""
+        """The pre-pass half of run() (sage_prepass) into the plan's buffers: INT8 codes, or (route
+        "codes16") the codes as fp16 values in self.codes16, or (route "fused") K alone."""
         B, Hq, Hkv, Sq, Skv, D = self.shape
         *_, qs = _dims(q, tensor_layout)
         *_, ks = _dims(k, tensor_layout)
         *_, vs = _dims(v, tensor_layout)
         qd = self.quant
+        flags = self.flags
+        qi, ki = qd.q_int8, qd.k_int8
+        if self.route == "fused":
+            flags |= N.SAGE_FLAG_FUSED_Q
+            qi = None
+        elif self.route == "codes16":
+            if self.codes16 is None:
+                self.codes16 = (torch.empty((B, Hq, Sq, D), dtype=torch.float16, device=self.device),
+                                torch.empty((B, Hkv, Skv, D), dtype=torch.float16, device=self.device))
+            flags |= N.SAGE_FLAG_CODES16
+            qi, ki = self.codes16
         rc = N.load().sage_prepass(
             _vp(q), _vp(k), _vp(v), _DTYPES[self.dtype], B, Hq, Hkv, Sq, Skv, D, N.strides3(*qs), N.strides3(*ks),
-            N.strides3(*vs), ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)), self.pv_mode,
-            self.flags | (N.SAGE_FLAG_FUSED_Q if self.fused_q else 0),
-            _vp(None if self.fused_q else qd.q_int8), _vp(None if self.fused_q else qd.q_scale), _vp(qd.k_int8),
-            _vp(qd.k_scale), _vp(qd.k_mean),
-            _vp(qd.v_fp8), _vp(qd.v_scale), _vp(self.ws), self.ws_bytes, _stream_ptr(self.device))
+            N.strides3(*vs), self._sm_scale(), self.pv_mode, flags, _vp(qi), _vp(qd.q_scale if qi is not None else None),
+            _vp(ki), _vp(qd.k_scale), _vp(qd.k_mean), _vp(qd.v_fp8), _vp(qd.v_scale), _vp(self.ws), self.ws_bytes,
+            _stream_ptr(self.device))
         N.check("sage_prepass", rc)
         return self.quant
 
     def attention(self, v, out, tensor_layout="HND", q=None):
-        """The attention half of run() over self.quant: sage_attn_fwd, or sage_attn_fwd_fused_q
-        (which needs ``q``) when the plan quantises Q in the attention kernel."""
+        """The attention half of run() over the prepass() results: sage_attn_fwd (route "int8"),
+        sage_attn_fwd_codes16 ("codes16") or sage_attn_fwd_fused_q ("fused", which needs ``q``)."""
         pv = "fp8" if self.pv_mode == N.SAGE_PV_FP8 else "16bit"
-        if not self.fused_q:
+        if self.route == "int8":
             return attn_fwd(self.quant, v, self.causal, pv=pv, out_dtype=self.dtype, tensor_layout=tensor_layout,
                             out=out)
-        if q is None:
-            raise ValueError("this plan quantises Q inside the attention kernel: pass q")
         B, Hq, Hkv, Sq, Skv, D = self.shape
         qd = self.quant
-        *_, qs = _dims(q, tensor_layout)
         *_, os_ = _dims(out, tensor_layout)
         if self.pv_mode == N.SAGE_PV_FP8:
             vv, vs = qd.v_fp8, (Skv * D * Hkv, Skv * D, D)
         else:
             vv = v
             *_, vs = _dims(v, tensor_layout)
-        rc = N.load().sage_attn_fwd_fused_q(
-            _vp(q), N.strides3(*qs), ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)),
-            _vp(qd.k_int8), _vp(qd.k_scale), _vp(vv), N.strides3(*vs), _vp(qd.v_scale), _vp(out), N.strides3(*os_),
-            _DTYPES[self.dtype], self.pv_mode, int(self.causal), B, Hq, Hkv, Sq, Skv, D, _vp(qd.q_int8),
-            _vp(qd.q_scale), _stream_ptr(self.device))
+        lib = N.load()
+        if self.route == "codes16":
+            if self.codes16 is None:
+                raise ValueError("call prepass() first")
+            rc = lib.sage_attn_fwd_codes16(
+                _vp(self.codes16[0]), _vp(qd.q_scale), _vp(self.codes16[1]), _vp(qd.k_scale), _vp(vv),
+                N.strides3(*vs), _vp(qd.v_scale), _vp(out), N.strides3(*os_), _DTYPES[self.dtype], self.pv_mode,
+                int(self.causal), B, Hq, Hkv, Sq, Skv, D, _stream_ptr(self.device))
+            N.check("sage_attn_fwd_codes16", rc)
+            return out
+        if q is None:
+            raise ValueError("this plan quantises Q inside the attention kernel: pass q")
+        *_, qs = _dims(q, tensor_layout)
+        rc = lib.sage_attn_fwd_fused_q(
+            _vp(q), N.strides3(*qs), self._sm_scale(), _vp(qd.k_int8), _vp(qd.k_scale), _vp(vv), N.strides3(*vs),
+            _vp(qd.v_scale), _vp(out), N.strides3(*os_), _DTYPES[self.dtype], self.pv_mode, int(self.causal), B, Hq,
+            Hkv, Sq, Skv, D, _vp(qd.q_int8), _vp(qd.q_scale), _stream_ptr(self.device))
         N.check("sage_attn_fwd_fused_q", rc)
         return out
 
@@ -277,11 +310,10 @@ class SagePlan:
         qd = self.quant
         rc = N.load().sage_run(
             _vp(q), _vp(k), _vp(v), _vp(out), _DTYPES[self.dtype], B, Hq, Hkv, Sq, Skv, D,
-            N.strides3(*qs), N.strides3(*ks), N.strides3(*vs), N.strides3(*os_), int(self.causal),
-            ctypes.c_float(0.0 if self.sm_scale is None else float(self.sm_scale)), self.pv_mode,
-            self.flags | (N.SAGE_FLAG_FUSED_Q if self.fused_q else N.SAGE_FLAG_PREPASS_Q),
-            _vp(qd.q_int8), _vp(qd.q_scale), _vp(qd.k_int8), _vp(qd.k_scale), _vp(qd.k_mean), _vp(qd.v_fp8),
-            _vp(qd.v_scale), _vp(self.ws), self.ws_bytes, _stream_ptr(self.device))
+            N.strides3(*qs), N.strides3(*ks), N.strides3(*vs), N.strides3(*os_), int(self.causal), self._sm_scale(),
+            self.pv_mode, self.flags | self.route_flag, _vp(qd.q_int8), _vp(qd.q_scale), _vp(qd.k_int8),
+            _vp(qd.k_scale), _vp(qd.k_mean), _vp(qd.v_fp8), _vp(qd.v_scale), _vp(self.ws), self.ws_bytes,
+            _stream_ptr(self.device))
         N.check("sage_run", rc)
         return out
 

@@ -164,8 +164,9 @@ def _out_and_v(bt: _Batch, q, v, out):
 def run_sage_attn_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q=None, max_seqlen_k=None, causal=False,
                          sm_scale=None, *, pv="16bit", smooth_k=True, out=None, fused_q=None):
     """run_sage_attn for packed sequences: q [total_q, Hq, D], k/v [total_k, Hkv, D] -> o like q.
-    A sequence with query rows but no keys gets o = 0. ``fused_q``: Q quantised inside the
-    attention kernel (None: at head_dim 128, as sage_run_varlen chooses); bit-identical output."""
+    A sequence with query rows but no keys gets o = 0. ``fused_q`` picks the operand route as
+    SagePlan does (None: Q quantised in the attention kernel at head_dim 128, fp16 codes at 64;
+    True: Q in the kernel; False: INT8 operands from the pre-pass)."""
     bt = _Batch(q, k, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal)
     vs, out, os_ = _out_and_v(bt, q, v, out)
     if bt.Tq == 0:
@@ -175,17 +176,18 @@ def run_sage_attn_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q=None,
     dev, D = bt.dev, bt.D
     pv_mode = _PV[pv]
     fp8 = pv_mode == N.SAGE_PV_FP8
-    fused_q = (D == 128) if fused_q is None else bool(fused_q)
-    q_i8 = None if fused_q else torch.empty((bt.Hq, bt.Tq, D), dtype=torch.int8, device=dev)
-    k_i8 = torch.empty((bt.Hkv, bt.Tk, D), dtype=torch.int8, device=dev)
-    q_scale = None if fused_q else torch.empty((bt.B, bt.Hq, (bt.max_q + 127) // 128), dtype=torch.float32,
-                                               device=dev)
+    route = ("fused" if D == 128 else "codes16") if fused_q is None else ("fused" if fused_q else "int8")
+    route_flag = {"fused": N.SAGE_FLAG_FUSED_Q, "int8": N.SAGE_FLAG_PREPASS_Q, "codes16": 0}[route]
+    q_i8 = torch.empty((bt.Hq, bt.Tq, D), dtype=torch.int8, device=dev) if route == "int8" else None
+    k_i8 = torch.empty((bt.Hkv, bt.Tk, D), dtype=torch.int8, device=dev) if route != "codes16" else None
+    q_scale = None if route == "fused" else torch.empty((bt.B, bt.Hq, (bt.max_q + 127) // 128), dtype=torch.float32,
+                                                        device=dev)
     k_scale = torch.empty((bt.B, bt.Hkv, (bt.max_k + 63) // 64), dtype=torch.float32, device=dev)
     k_mean = torch.empty((bt.B, bt.Hkv, D), dtype=torch.float32, device=dev) if smooth_k else None
     v_fp8 = torch.empty((bt.Hkv, bt.Tk, D), dtype=torch.uint8, device=dev) if fp8 else None
     v_scale = torch.empty((bt.B, bt.Hkv, D), dtype=torch.float32, device=dev) if fp8 else None
-    flags = (N.SAGE_FLAG_SMOOTH_K if smooth_k else 0) | (N.SAGE_FLAG_FUSED_Q if fused_q else N.SAGE_FLAG_PREPASS_Q)
-    ws_n = workspace_bytes(bt.B, bt.Hkv, bt.max_k, D, pv, smooth_k)
+    flags = (N.SAGE_FLAG_SMOOTH_K if smooth_k else 0) | route_flag
+    ws_n = int(N.load().sage_workspace_bytes(bt.B, bt.Hkv, bt.max_k, D, pv_mode, flags))
     ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         rc = N.load().sage_run_varlen(
