@@ -246,7 +246,12 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
   p.n_k = want_km ? 0 : (int)n_k;
   p.n_v = 0;
   const int64_t grid_a = (int64_t)p.n_q + p.n_stat + p.n_k;
-  if (grid_a > 0) {
+  if (grid_a > 0 && grid_a == p.n_stat && !want_v) {
+    // K statistics alone (Q quantised in the attention kernel): the lighter statistics kernel
+    if (vl) sage::kstats_kernel<D, T, true><<<(unsigned)grid_a, sage::kQuantThreads, 0, st>>>(p);
+    else sage::kstats_kernel<D, T, false><<<(unsigned)grid_a, sage::kQuantThreads, 0, st>>>(p);
+    SAGE_CUDA_TRY(cudaGetLastError());
+  } else if (grid_a > 0) {
     launch_prepass_kernel<D, T>(p, grid_a, vl != nullptr, c16 != nullptr, st);
     SAGE_CUDA_TRY(cudaGetLastError());
   }
