@@ -201,6 +201,21 @@ void launch_prepass_kernel(const sage::PrepassParams& p, int64_t grid, bool pack
   else sage::prepass_kernel<D, T, false><<<g, sage::kQuantThreads, 0, st>>>(p);
 }
 
+// K quantisation alone (launch B without V blocks): the 128-thread kernel.
+template <int D, typename T>
+void launch_kquant_kernel(const sage::PrepassParams& p, bool packed, bool c16, cudaStream_t st) {
+  const dim3 g((unsigned)p.n_k);
+  if constexpr (D == 64) {
+    if (c16) {
+      if (packed) sage::kquant_kernel<D, T, true, true><<<g, sage::kKQuantThreads, 0, st>>>(p);
+      else sage::kquant_kernel<D, T, false, true><<<g, sage::kKQuantThreads, 0, st>>>(p);
+      return;
+    }
+  }
+  if (packed) sage::kquant_kernel<D, T, true, false><<<g, sage::kKQuantThreads, 0, st>>>(p);
+  else sage::kquant_kernel<D, T, false, false><<<g, sage::kKQuantThreads, 0, st>>>(p);
+}
+
 template <int D, typename T>
 int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                    int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs, float q_mult, bool smooth,
@@ -268,7 +283,11 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
     p.n_k = want_km ? (int)n_k : 0;
     p.n_v = (int)n_v;
     const int64_t grid_b = (int64_t)p.n_k + p.n_v;
-    if (grid_b > 0) {
+    if (p.n_k > 0 && p.n_v == 0) {
+      p.n_k = (int)(B * Hkv * cdiv(p.nkb, sage::kKQuantBlocks<D>));
+      launch_kquant_kernel<D, T>(p, vl != nullptr, c16 != nullptr, st);
+      SAGE_CUDA_TRY(cudaGetLastError());
+    } else if (grid_b > 0) {
       launch_prepass_kernel<D, T>(p, grid_b, vl != nullptr, c16 != nullptr, st);
       SAGE_CUDA_TRY(cudaGetLastError());
     }

@@ -85,9 +85,9 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 
 // Block-wide maxima of N values per thread in one reduction round; red holds
 // N * (kQuantThreads / 32) floats. Called once per CTA.
-template <int N>
+template <int N, int NT = kQuantThreads>
 __device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
-  constexpr int W = kQuantThreads / 32;
+  constexpr int W = NT / 32;
 #pragma unroll
   for (int n = 0; n < N; ++n)
 #pragma unroll
@@ -178,11 +178,11 @@ struct PrepassParams {
 };
 
 // ---------------------------------------------------------------- roles
-// NSUB consecutive scale blocks of BLK rows, all rows loaded up front.
-template <int D, typename T, int BLK, int NSUB, bool PACKED, bool C16>
+// NSUB consecutive scale blocks of BLK rows, all rows loaded up front, by a CTA of NT threads.
+template <int D, typename T, int BLK, int NSUB, bool PACKED, bool C16, int NT = kQuantThreads>
 __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta, bool isq, float* red) {
   constexpr int TPR = D / 8;                 // threads per row (8 channels each)
-  constexpr int RPP = kQuantThreads / TPR;   // rows per pass
+  constexpr int RPP = NT / TPR;              // rows per pass
   constexpr int PPB = BLK / RPP;             // passes per scale block
   constexpr int NP = NSUB * PPB;             // passes
   const int g = threadIdx.x % TPR, r = threadIdx.x / TPR;
@@ -240,7 +240,7 @@ __device__ __forceinline__ void quant_block_role(const PrepassParams& p, int cta
 #pragma unroll
     for (int i = 0; i < NP; ++i) amax[i / PPB] = fmaxf(amax[i / PPB], Half8<T>::absmax(raw[i]));
   }
-  block_max_n<NSUB>(amax, red);
+  block_max_n<NSUB, NT>(amax, red);
   float scale[NSUB], rcp[NSUB];
 #pragma unroll
   for (int b = 0; b < NSUB; ++b) {
@@ -447,6 +447,22 @@ __global__ void __launch_bounds__(kQuantThreads, 4) kstats_kernel(PrepassParams 
   __shared__ double sum_red[RPP][D];
   __shared__ float max_red[RPP][D];
   stats_role<D, T, PACKED, 8, true>(p, blockIdx.x, sum_red, max_red);
+}
+
+// K quantisation alone (launch B when no V block needs e4m3 codes): CTAs of 128 threads, each
+// thread with eight 16-byte rows in flight (one 64-row block at head_dim 128, two at 64), and at
+// most 64 registers so that eight CTAs share an SM. The combined kernel's CTAs carry the 24 KB
+// statistics buffers and 80 registers (three per SM, four rows in flight per thread); on the
+// H8K shape this launch streams K at ~5.7 TB/s against ~3.2 TB/s there (pre-pass 97 -> 80 us,
+// C3 191 -> 148 us, bit-identical codes).
+constexpr int kKQuantThreads = 128;
+template <int D> constexpr int kKQuantBlocks = (D == 64) ? 2 : 1;  // 64-row blocks per CTA
+template <int D, typename T, bool PACKED, bool C16>
+__global__ void __launch_bounds__(kKQuantThreads, 8) kquant_kernel(PrepassParams p) {
+  __shared__ float red[kKQuantBlocks<D> * (kKQuantThreads / 32)];
+  // reverse head order, as in the combined kernel: the statistics launch read the last heads last
+  quant_block_role<D, T, 64, kKQuantBlocks<D>, PACKED, C16, kKQuantThreads>(p, p.n_k - 1 - (int)blockIdx.x, false,
+                                                                           red);
 }
 
 struct FinalizeParams {
