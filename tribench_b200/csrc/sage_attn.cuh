@@ -530,25 +530,6 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH, C16>::NUM_THREADS, 1
       tc_fence_after();
       SAGE_T_MARK(0)
       float b[128];
-#ifdef SAGE_SPLIT_SLOAD
-      {
-        // four 32-column loads, each one's bias step overlapping the next one's flight
-        uint32_t sr[4][32];
-        tmem_ld32_async(s_tmem, sr[0]);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          tmem_wait_ld32(sr[q4]);
-          if (q4 < 3) tmem_ld32_async(s_tmem + 32 * (q4 + 1), sr[q4 + 1]);
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            b[32 * q4 + c] = __uint_as_float((C::QK_F16 || C::PRE_BIAS) ? sr[q4][c] : sr[q4][c] + 0x4B400000u);
-        }
-        if constexpr (C::SEP_P) {
-          tc_fence_before();
-          mbar_arrive(bar_sload + t);  // S_t(j) is in registers: QK_t(j+1) may overwrite it
-        }
-      }
-#else
       {
         uint32_t sr[128];
         tmem_ld128_sync(s_tmem, sr);
@@ -561,7 +542,6 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH, C16>::NUM_THREADS, 1
 #pragma unroll
         for (int c = 0; c < 128; ++c) b[c] = __uint_as_float((C::QK_F16 || C::PRE_BIAS) ? sr[c] : sr[c] + 0x4B400000u);
       }
-#endif
       SAGE_T_MARK(1)
       const int key0 = j * C::BN;
       if ((key0 + C::BN > Skv) || (p.causal && key0 + C::BN - 1 > r0)) {

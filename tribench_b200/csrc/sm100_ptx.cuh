@@ -259,25 +259,6 @@ __device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, uint32_t (&r)[32]
       : "r"(taddr)
       : "memory");
 }
-// Split form for pipelined loads: tmem_ld32_async issues the load; tmem_wait_ld32 waits for
-// it and passes the same registers through as read-write operands, so every consumer reads
-// values defined after the wait (nothing can be hoisted above it). Only one load may be
-// outstanding between the two (the wait covers every earlier tcgen05.ld of the thread).
-__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : SAGE_R8(0), SAGE_R8(8), SAGE_R8(16), SAGE_R8(24)
-      : "r"(taddr)
-      : "memory");
-}
-#define SAGE_RW8(i) "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), \
-                    "+r"(r[i + 4]), "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7])
-__device__ __forceinline__ void tmem_wait_ld32(uint32_t (&r)[32]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" : SAGE_RW8(0), SAGE_RW8(8), SAGE_RW8(16), SAGE_RW8(24) : : "memory");
-}
-#undef SAGE_RW8
 #define SAGE_R8O(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), \
                     "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
 __device__ __forceinline__ void tmem_ld128_sync(uint32_t taddr, uint32_t (&r)[128]) {
