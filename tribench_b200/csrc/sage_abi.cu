@@ -216,6 +216,19 @@ void launch_kquant_kernel(const sage::PrepassParams& p, bool packed, bool c16, c
   else sage::kquant_kernel<D, T, false, false><<<g, sage::kKQuantThreads, 0, st>>>(p);
 }
 
+// Q quantisation alone at head_dim 64: the 128-thread kernel, one block per CTA.
+template <typename T>
+void launch_qquant_kernel(const sage::PrepassParams& p, bool packed, bool c16, cudaStream_t st) {
+  const dim3 g((unsigned)p.n_q);
+  if (c16) {
+    if (packed) sage::qquant_kernel<T, true, true><<<g, sage::kKQuantThreads, 0, st>>>(p);
+    else sage::qquant_kernel<T, false, true><<<g, sage::kKQuantThreads, 0, st>>>(p);
+  } else {
+    if (packed) sage::qquant_kernel<T, true, false><<<g, sage::kKQuantThreads, 0, st>>>(p);
+    else sage::qquant_kernel<T, false, false><<<g, sage::kKQuantThreads, 0, st>>>(p);
+  }
+}
+
 template <int D, typename T>
 int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                    int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs, float q_mult, bool smooth,
@@ -255,8 +268,20 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
     p.stat_k = want_km ? 1 : 0;
     p.stat_v = want_v ? 1 : 0;
   }
+  // Q blocks at head_dim 64 in their own 128-thread launch (every Q block the pre-pass sees at
+  // 64: the fp16-code and INT8 routes)
+  bool q_done = false;
+  if constexpr (D == 64) {
+    if (n_q > 0) {
+      p.n_q = (int)(B * Hq * p.nqb);
+      p.n_stat = p.n_k = p.n_v = 0;
+      launch_qquant_kernel<T>(p, vl != nullptr, c16 != nullptr, st);
+      SAGE_CUDA_TRY(cudaGetLastError());
+      q_done = true;
+    }
+  }
   // launch A: Q blocks and statistics chunks (and K blocks when K needs no statistics)
-  p.n_q = (int)n_q;
+  p.n_q = q_done ? 0 : (int)n_q;
   p.n_stat = (int)n_stat;
   p.n_k = want_km ? 0 : (int)n_k;
   p.n_v = 0;
@@ -283,10 +308,19 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
     p.n_k = want_km ? (int)n_k : 0;
     p.n_v = (int)n_v;
     const int64_t grid_b = (int64_t)p.n_k + p.n_v;
-    if (p.n_k > 0 && p.n_v == 0) {
+    if (p.n_k > 0) {
+      // K blocks in the 128-thread kernel, then V blocks (if any) in the combined one
+      const int n_v_b = p.n_v;
       p.n_k = (int)(B * Hkv * cdiv(p.nkb, sage::kKQuantBlocks<D>));
+      p.n_v = 0;
       launch_kquant_kernel<D, T>(p, vl != nullptr, c16 != nullptr, st);
       SAGE_CUDA_TRY(cudaGetLastError());
+      if (n_v_b > 0) {
+        p.n_k = 0;
+        p.n_v = n_v_b;
+        launch_prepass_kernel<D, T>(p, n_v_b, vl != nullptr, c16 != nullptr, st);
+        SAGE_CUDA_TRY(cudaGetLastError());
+      }
     } else if (grid_b > 0) {
       launch_prepass_kernel<D, T>(p, grid_b, vl != nullptr, c16 != nullptr, st);
       SAGE_CUDA_TRY(cudaGetLastError());

@@ -465,6 +465,14 @@ __global__ void __launch_bounds__(kKQuantThreads, 8) kquant_kernel(PrepassParams
                                                                            red);
 }
 
+// Q quantisation alone at head_dim 64 (the launch before the statistics): the same 128-thread
+// shape, one 128-row block per CTA (eight 16-byte rows in flight per thread).
+template <typename T, bool PACKED, bool C16>
+__global__ void __launch_bounds__(kKQuantThreads, 8) qquant_kernel(PrepassParams p) {
+  __shared__ float red[kKQuantThreads / 32];
+  quant_block_role<64, T, 128, 1, PACKED, C16, kKQuantThreads>(p, (int)blockIdx.x, true, red);
+}
+
 struct FinalizeParams {
   const double* ksum_part;  // nullable
   const float* vmax_part;   // nullable
