@@ -150,11 +150,14 @@ struct AttnCfg {
   // P <= 2^(P_SHIFT + LAZY) = 2^8.8 ~ 445.7 below e4m3's largest finite value, 448.
   static constexpr float LAZY = (PV == kPvE4M3) ? 0.8f : 8.0f;
   static constexpr float P_SHIFT = (PV == kPvE4M3) ? 8.0f : 0.0f;
-  // Exponentials per 32 columns computed by the FMA-pipe polynomial instead of MUFU.ex2.
+  // Exponentials per 32 columns computed by the FMA-pipe polynomial instead of MUFU.ex2, by
+  // measurement: 12 at head_dim 128 and for the flash variant; 8 for the INT8 scheme at 64
+  // (same-call A/B against 12: s4k_d64 step 842 -> 803 us, s8k_d64 1549 -> 1479 us, C4
+  // 1851 -> 1799 us; 0, 4 and 6 were slower than 8; the flash variant is 3-4 % slower at 8).
 #ifdef SAGE_EMU_PER_32
   static constexpr int EMU = SAGE_EMU_PER_32;
 #else
-  static constexpr int EMU = 12;
+  static constexpr int EMU = (D == 64 && !FLASH) ? 8 : 12;
 #endif
 };
 
