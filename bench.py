@@ -58,7 +58,7 @@ def parse():
                     choices=["h8k", "c2", "c3", "c4", "c5", "s4k_d64", "s8k_d64", "fa_s4k_d64", "fa_s8k_d64"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--e2e-chunks", type=int, default=8, help="head chunks of the host pipeline (e2e)")
+    ap.add_argument("--e2e-chunks", type=int, default=16, help="head chunks of the host pipeline (e2e)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--waves", type=int, default=8, help="head waves per rank (sharded c5 workload)")

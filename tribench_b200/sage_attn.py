@@ -355,7 +355,7 @@ class HostPipeline:
     returns, the caller's stream is ordered after the last device -> host copy.
     """
 
-    def __init__(self, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, dtype, device, *, chunks=8,
+    def __init__(self, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, dtype, device, *, chunks=16,
                  pv="16bit", smooth_k=True, causal=False, sm_scale=None):
         if heads_kv <= 0 or heads_q % heads_kv:
             raise ValueError(f"heads_q ({heads_q}) must be a multiple of heads_kv ({heads_kv})")
