@@ -108,7 +108,10 @@ def read_traffic() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 100 ms while the warm-up and timed steps run."""
+    """nvidia-smi clocks/throttle reasons sampled every INTERVAL_MS while the warm-up and timed
+    steps run; the summary's sm_mhz is the median over those samples (under load)."""
+
+    INTERVAL_MS = 20
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -124,7 +127,7 @@ class ClockSampler:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+                 "-lms", str(self.INTERVAL_MS)], stdout=self.file, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -160,7 +163,8 @@ class ClockSampler:
                     reasons.add(n)
         loaded = [s for s, p in zip(sm, power) if p > 300.0] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm),
+                "reasons": sorted(reasons), "samples": len(sm), "samples_under_load": len(loaded),
+                "interval_ms": self.INTERVAL_MS, "over": "warm-up + timed steps (median of samples above 300 W)",
                 "power_w_max": max(power) if power else None}
 
 

@@ -22,6 +22,12 @@
  *   k_mean  fp32  [B, Hkv, D]           per-channel token mean of K (smoothing only)
  *   v_fp8   e4m3  [B, Hkv, Skv, D]      per-channel scaled V (FP8 P.V mode only)
  *   v_scale fp32  [B, Hkv, D]
+ *
+ * Output aliasing: every entry point that writes an attention output o rejects, with
+ * SAGE_ERR_INVALID_ARG and before any CUDA call, an o whose bytes overlap k, v, an
+ * intermediate or the workspace, or overlap q other than as the identical view (same base
+ * pointer and strides; in place, o = q, is allowed). The check compares the byte ranges the
+ * tensors span, so an o interleaved with k or v inside one packed buffer is rejected too.
  */
 #ifndef SAGE_SM100_H_
 #define SAGE_SM100_H_
@@ -118,9 +124,12 @@ int sage_per_block_int8(const void* q, const void* k, int dtype,
  * process exits); sizes needing more (batch * heads_kv * ceil(seq_kv / 512) * head_dim above
  * 524288) are rejected with SAGE_ERR_INVALID_ARG. The caller still passes every input and
  * output. The first call on a device looks up the scratch's device address (no allocation),
- * so make that first call before any stream capture. Every call on a device shares the one
- * scratch array: calls that overlap on the GPU (other streams, other threads) race and must be
- * serialised by the caller. No counterpart in the reference.
+ * so make that first call before any stream capture. The address is cached per device ordinal
+ * for the life of the process: after cudaDeviceReset (which destroys the context holding the
+ * array) the cached address is stale, so do not call this entry point again in that process.
+ * Every call on a device shares the one scratch array: calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialised by the caller. No counterpart in the
+ * reference.
  */
 int sage_per_block_int8_noalloc(const void* q, const void* k, int dtype,
                                 int64_t batch, int64_t heads_q, int64_t heads_kv,
@@ -213,8 +222,8 @@ int sage_prepass(const void* q, const void* k, const void* v, int dtype,
  * sage_attn_fwd_fused_q) and q_i8 / q_scale are optional outputs; the result is bit-identical
  * to the pre-pass route (sage_prepass + sage_attn_fwd). At head_dim 64 (unless a flag above
  * says otherwise) the pre-pass stores the codes as fp16 values, Q's in o itself (each CTA
- * reads its own query rows before it writes the same rows of o, so o must not overlap k or v)
- * and K's in the workspace, and QK^T runs on them as a kind::f16 MMA (sage_prepass with
+ * reads its own query rows before it writes the same rows of o; o overlapping k or v is
+ * rejected, see "Output aliasing" above) and K's in the workspace, and QK^T runs on them as a kind::f16 MMA (sage_prepass with
  * SAGE_FLAG_CODES16 + sage_attn_fwd_codes16): q_i8 / k_i8 are then not used (may be NULL), the
  * scores are the INT8 MMA's exactly, and the output matches the INT8 route to float rounding.
  */

@@ -156,16 +156,22 @@ def test_flash_rejects_bad_arguments_before_any_cuda_call():
     assert call(q=None) == N.SAGE_ERR_INVALID_ARG
 
 
+def _distinct(n, size=1 << 12):
+    """n non-overlapping 16-byte aligned host buffers (kept alive by the returned list)."""
+    bufs = [_dummy(size) for _ in range(n)]
+    return [b for b, _ in bufs], [ptr for _, ptr in bufs]
+
+
 def test_fused_q_makes_q_buffers_optional():
     """Host-side validation (no device here): NULL q_i8 / q_scale are rejected unless Q is
     quantised in the attention kernel."""
     lib = N.load()
-    keep, p = _dummy()
+    keep, (q, k, v, o, ki, ksc, p) = _distinct(7)
     s = N.strides3(8 * 128, 8 * 128, 128)
 
     def run(flags, qi):
-        return lib.sage_run(p, p, p, p, N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 128, s, s, s, s, 0, 0.0, N.SAGE_PV_16BIT,
-                            flags, qi, qi, p, p, None, None, None, None, 0, None)
+        return lib.sage_run(q, k, v, o, N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 128, s, s, s, s, 0, 0.0, N.SAGE_PV_16BIT,
+                            flags, qi, qi, ki, ksc, None, None, None, None, 0, None)
 
     assert run(N.SAGE_FLAG_PREPASS_Q, None) == N.SAGE_ERR_INVALID_ARG and "NULL" in lib.sage_last_error().decode()
     # fused (the flag, or head_dim 128 by default): the arguments pass validation and the call
@@ -178,3 +184,53 @@ def test_fused_q_makes_q_buffers_optional():
                                          N.SAGE_PV_16BIT, flags, None, None, p, p, None, None, None, None, 0, None)
     assert pre(0) == N.SAGE_ERR_INVALID_ARG
     assert pre(N.SAGE_FLAG_FUSED_Q) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)
+
+
+def test_output_aliasing_is_rejected_before_any_cuda_call():
+    """Host-side validation (no device here): an output buffer that shares bytes with k, v, an
+    intermediate or the workspace, or overlaps q as a different view, is rejected with
+    SAGE_ERR_INVALID_ARG (the head_dim-64 route of sage_run parks Q's codes in o while K and V
+    are still to be read). o = q as the identical view passes validation (in-place is safe:
+    each CTA reads its query rows before writing the same rows of o)."""
+    lib = N.load()
+    keep, (q, k, v, o, qi, qsc, ki, ksc, ws) = _distinct(9, size=1 << 14)
+    s = N.strides3(8 * 128, 8 * 128, 128)  # [1, 1, 8, 128] fp16: 2048 bytes
+    off = lambda ptr, n: ctypes.c_void_p(ptr.value + n)
+
+    def run(o_ptr, head_dim=128, flags=N.SAGE_FLAG_SMOOTH_K | N.SAGE_FLAG_PREPASS_Q, q_ptr=q, os=s):
+        return lib.sage_run(q_ptr, k, v, o_ptr, N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, head_dim, s, s, s, os, 0, 0.0,
+                            N.SAGE_PV_16BIT, flags, qi, qsc, ki, ksc, off(ws, 4096), None, None, ws, 4096, None)
+
+    def msg():
+        return lib.sage_last_error().decode()
+
+    assert run(o) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)  # disjoint buffers: stops at the missing device
+    assert run(off(k, 1024)) == N.SAGE_ERR_INVALID_ARG and "overlaps k" in msg()
+    assert run(off(v, 16)) == N.SAGE_ERR_INVALID_ARG and "overlaps v" in msg()
+    assert run(off(ki, 512)) == N.SAGE_ERR_INVALID_ARG and "overlaps k_i8" in msg()
+    assert run(off(ws, 0)) == N.SAGE_ERR_INVALID_ARG and "overlaps workspace" in msg()
+    assert run(off(q, 256)) == N.SAGE_ERR_INVALID_ARG and "overlaps q" in msg()
+    # the same base as q but other strides is a different view
+    assert run(q, os=N.strides3(8 * 256, 8 * 128, 256)) == N.SAGE_ERR_INVALID_ARG and "overlaps q" in msg()
+    # in place (o = q, same strides) is allowed, on either route
+    assert run(q) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)
+    assert run(q, head_dim=64, flags=N.SAGE_FLAG_SMOOTH_K) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)
+    assert run(off(k, 64), head_dim=64, flags=N.SAGE_FLAG_SMOOTH_K) == N.SAGE_ERR_INVALID_ARG
+
+    # the split entry point and the flash pack check the same way
+    rc = lib.sage_attn_fwd(qi, qsc, ki, ksc, v, s, None, off(ki, 128), s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 1, 1,
+                           1, 8, 8, 128, None)
+    assert rc == N.SAGE_ERR_INVALID_ARG and "overlaps k_i8" in msg()
+    rc = lib.sage_flash_attn_fwd(q, k, v, off(v, 2032), N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 128, s, s, s, s, 0, 0.0, None)
+    assert rc == N.SAGE_ERR_INVALID_ARG and "overlaps v" in msg()
+    # one byte past v's last element is no overlap
+    rc = lib.sage_flash_attn_fwd(q, k, v, off(v, 2048), N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 128, s, s, s, s, 0, 0.0, None)
+    assert rc not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)
+
+    # packed sequences: o [total_q, H, D] against k
+    cu_keep, cu = _dummy(64)
+    s2 = N.strides2(128, 128)
+    rc = lib.sage_run_varlen(q, k, v, off(k, 1024), N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 8, 8, 128, cu, cu, s2, s2, s2, s2,
+                             0, 0.0, N.SAGE_PV_16BIT, N.SAGE_FLAG_PREPASS_Q, qi, qsc, ki, ksc, None, None, None, None,
+                             0, None)
+    assert rc == N.SAGE_ERR_INVALID_ARG and "overlaps k" in msg()

@@ -117,6 +117,73 @@ int check_shape(int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// ---------------------------------------------------------------- output aliasing
+// Byte range [lo, hi) a buffer covers. A strided [B, H, S, D] tensor (element strides {batch,
+// head, seq}, D contiguous) covers everything between its first and its last element.
+struct Span {
+  uintptr_t lo = 0, hi = 0;
+};
+Span buffer_span(const void* p, size_t bytes) {
+  const uintptr_t lo = reinterpret_cast<uintptr_t>(p);
+  return p ? Span{lo, lo + bytes} : Span{};
+}
+Span tensor_span(const void* p, const int64_t* s, int64_t B, int64_t H, int64_t S, int64_t D, int elt) {
+  if (!p || !s) return Span{};
+  const int64_t last = (B - 1) * s[0] + (H - 1) * s[1] + (S - 1) * s[2] + D;  // elements
+  return buffer_span(p, static_cast<size_t>(last) * static_cast<size_t>(elt));
+}
+bool spans_overlap(const Span& a, const Span& b) { return a.lo < a.hi && b.lo < b.hi && a.lo < b.hi && b.lo < a.hi; }
+struct NamedSpan {
+  const char* name;
+  Span span;
+};
+
+// The output o is written while the call still reads its other operands (another CTA's K/V
+// tiles, the intermediates, and on the head_dim-64 route of sage_run Q's codes parked in o
+// itself), so o must not share a byte with any of them. The one permitted overlap is o = q as
+// the identical view (same base and strides): every CTA reads its own query rows before it
+// writes the same rows of o. The check compares byte ranges, so it is conservative: o
+// interleaved with k or v inside one packed buffer is rejected too.
+int check_out_alias(const void* o, const int64_t* os, const Span& o_span, const void* q, const int64_t* qs,
+                    const Span& q_span, const NamedSpan* others, int n_others) {
+  if (spans_overlap(o_span, q_span)) {
+    const bool same_view = o == q && os && qs && os[0] == qs[0] && os[1] == qs[1] && os[2] == qs[2];
+    if (!same_view)
+      return fail(SAGE_ERR_INVALID_ARG,
+                  "o overlaps q without being the same view (same base pointer and strides): the result "
+                  "would be corrupted");
+  }
+  for (int i = 0; i < n_others; ++i)
+    if (spans_overlap(o_span, others[i].span))
+      return fail(SAGE_ERR_INVALID_ARG, "o overlaps %s: the result would be corrupted", others[i].name);
+  return SAGE_OK;
+}
+
+// check_out_alias over everything an attention call reads: q (identical view allowed), k, v
+// and the caller's intermediates (NULL ones are skipped). q_rows / k_rows = rows of the token
+// axis summed over the batch (dense: B * S; packed sequences: the token counts); nqb / nkb =
+// scale blocks per (batch, head).
+int check_attn_alias(const void* o, const int64_t* os, const Span& o_span, const void* q, const int64_t* qs,
+                     const Span& q_span, const Span& k_span, const Span& v_span, int64_t B, int64_t Hq, int64_t Hkv,
+                     int64_t q_rows, int64_t k_rows, int64_t nqb, int64_t nkb, int64_t D, const void* q_i8,
+                     const void* q_scale, const void* k_i8, const void* k_scale, const void* k_mean,
+                     const void* v_fp8, const void* v_scale, const void* ws, size_t ws_bytes) {
+  const size_t f4 = sizeof(float);
+  const NamedSpan others[] = {
+      {"k", k_span},
+      {"v", v_span},
+      {"q_i8", buffer_span(q_i8, static_cast<size_t>(Hq * q_rows * D))},
+      {"q_scale", buffer_span(q_scale, static_cast<size_t>(B * Hq * nqb) * f4)},
+      {"k_i8", buffer_span(k_i8, static_cast<size_t>(Hkv * k_rows * D))},
+      {"k_scale", buffer_span(k_scale, static_cast<size_t>(B * Hkv * nkb) * f4)},
+      {"k_mean", buffer_span(k_mean, static_cast<size_t>(B * Hkv * D) * f4)},
+      {"v_fp8", buffer_span(v_fp8, static_cast<size_t>(Hkv * k_rows * D))},
+      {"v_scale", buffer_span(v_scale, static_cast<size_t>(B * Hkv * D) * f4)},
+      {"workspace", buffer_span(ws, ws_bytes)},
+  };
+  return check_out_alias(o, os, o_span, q, qs, q_span, others, static_cast<int>(sizeof(others) / sizeof(others[0])));
+}
+
 size_t ws_ksum_bytes(int64_t B, int64_t Hkv, int64_t Skv, int64_t D) {
   return static_cast<size_t>(B * Hkv * cdiv(Skv, sage::kStatsChunk) * D) * sizeof(double);
 }
@@ -651,6 +718,16 @@ int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, 
   if (!q_i8 || !q_scale || !k_i8 || !k_scale || !v || !o) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q_i8) || !aligned16(k_i8) || !aligned16(v) || !aligned16(o))
     return fail(SAGE_ERR_INVALID_ARG, "q_i8/k_i8/v/o must be 16-byte aligned");
+  {
+    const bool fp8 = pv_mode == SAGE_PV_FP8;
+    const Span vsp = fp8 ? buffer_span(v, static_cast<size_t>(batch * heads_kv * seq_kv * head_dim))
+                         : tensor_span(v, v_strides, batch, heads_kv, seq_kv, head_dim, 2);
+    if (int rc = check_attn_alias(o, o_strides, tensor_span(o, o_strides, batch, heads_q, seq_q, head_dim, 2), nullptr,
+                                  nullptr, Span{}, Span{}, vsp, batch, heads_q, heads_kv, batch * seq_q, batch * seq_kv,
+                                  cdiv(seq_q, 128), cdiv(seq_kv, 64), head_dim, q_i8, q_scale, k_i8, k_scale, nullptr,
+                                  nullptr, fp8 ? v_scale : nullptr, nullptr, 0))
+      return rc;
+  }
   if (int rc = check_arch()) return rc;
   return attn_impl(q_i8, q_scale, k_i8, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal, batch,
                    heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream));
@@ -679,6 +756,17 @@ int sage_attn_fwd_fused_q(const void* q, const int64_t q_strides[3], float sm_sc
     return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q) || !aligned16(k_i8) || !aligned16(v) || !aligned16(o) || (q_i8_out && !aligned16(q_i8_out)))
     return fail(SAGE_ERR_INVALID_ARG, "q/k_i8/v/o/q_i8_out must be 16-byte aligned");
+  {
+    const bool fp8 = pv_mode == SAGE_PV_FP8;
+    const Span vsp = fp8 ? buffer_span(v, static_cast<size_t>(batch * heads_kv * seq_kv * head_dim))
+                         : tensor_span(v, v_strides, batch, heads_kv, seq_kv, head_dim, 2);
+    if (int rc = check_attn_alias(o, o_strides, tensor_span(o, o_strides, batch, heads_q, seq_q, head_dim, 2), q,
+                                  q_strides, tensor_span(q, q_strides, batch, heads_q, seq_q, head_dim, 2), Span{}, vsp,
+                                  batch, heads_q, heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, 128),
+                                  cdiv(seq_kv, 64), head_dim, q_i8_out, q_scale_out, k_i8, k_scale, nullptr, nullptr,
+                                  fp8 ? v_scale : nullptr, nullptr, 0))
+      return rc;
+  }
   if (int rc = check_arch()) return rc;
   const FusedQ fq{q, q_strides, q_multiplier(sm_scale, head_dim), q_i8_out, q_scale_out};
   return attn_impl(nullptr, nullptr, k_i8, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal,
@@ -707,8 +795,21 @@ int sage_attn_fwd_codes16(const void* q_c16, const float* q_scale, const void* k
   if (!q_c16 || !q_scale || !k_c16 || !k_scale || !v || !o) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q_c16) || !aligned16(k_c16) || !aligned16(v) || !aligned16(o))
     return fail(SAGE_ERR_INVALID_ARG, "q_c16/k_c16/v/o must be 16-byte aligned");
-  if (int rc = check_arch()) return rc;
   const int64_t qcs[3] = {heads_q * seq_q * head_dim, seq_q * head_dim, head_dim};
+  {
+    // q_c16 may be o itself (contiguous o, as sage_run arranges it); k_c16 holds 2-byte codes
+    const bool fp8 = pv_mode == SAGE_PV_FP8;
+    const Span vsp = fp8 ? buffer_span(v, static_cast<size_t>(batch * heads_kv * seq_kv * head_dim))
+                         : tensor_span(v, v_strides, batch, heads_kv, seq_kv, head_dim, 2);
+    const Span ksp = buffer_span(k_c16, static_cast<size_t>(batch * heads_kv * seq_kv * head_dim) * 2);
+    if (int rc = check_attn_alias(o, o_strides, tensor_span(o, o_strides, batch, heads_q, seq_q, head_dim, 2), q_c16,
+                                  qcs, tensor_span(q_c16, qcs, batch, heads_q, seq_q, head_dim, 2), ksp, vsp, batch,
+                                  heads_q, heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, 128), cdiv(seq_kv, 64),
+                                  head_dim, nullptr, q_scale, nullptr, k_scale, nullptr, nullptr,
+                                  fp8 ? v_scale : nullptr, nullptr, 0))
+      return rc;
+  }
+  if (int rc = check_arch()) return rc;
   const Codes16 c16{static_cast<__half*>(const_cast<void*>(q_c16)), qcs,
                     static_cast<__half*>(const_cast<void*>(k_c16))};
   return attn_impl(nullptr, q_scale, nullptr, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal,
@@ -813,6 +914,14 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
                 (long long)seq_kv);
   if (int rc = check_strides("o", o_strides)) return rc;
   if (!o || !aligned16(o)) return fail(SAGE_ERR_INVALID_ARG, "o must be a 16-byte aligned pointer");
+  if (int rc = check_attn_alias(o, o_strides, tensor_span(o, o_strides, batch, heads_q, seq_q, head_dim, 2), q,
+                                q_strides, tensor_span(q, q_strides, batch, heads_q, seq_q, head_dim, 2),
+                                tensor_span(k, k_strides, batch, heads_kv, seq_kv, head_dim, 2),
+                                tensor_span(v, v_strides, batch, heads_kv, seq_kv, head_dim, 2), batch, heads_q,
+                                heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, 128), cdiv(seq_kv, 64), head_dim,
+                                q_i8, q_scale, k_i8, k_scale, k_mean, pv_mode == SAGE_PV_FP8 ? v_fp8 : nullptr,
+                                pv_mode == SAGE_PV_FP8 ? v_scale : nullptr, workspace, workspace_bytes))
+    return rc;
   if (int rc = check_arch()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool fp8 = pv_mode == SAGE_PV_FP8;
@@ -857,6 +966,13 @@ int sage_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, in
   if (!q || !k || !v || !o) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o must be 16-byte aligned");
+  if (int rc = check_attn_alias(o, o_strides, tensor_span(o, o_strides, batch, heads_q, seq_q, head_dim, 2), q,
+                                q_strides, tensor_span(q, q_strides, batch, heads_q, seq_q, head_dim, 2),
+                                tensor_span(k, k_strides, batch, heads_kv, seq_kv, head_dim, 2),
+                                tensor_span(v, v_strides, batch, heads_kv, seq_kv, head_dim, 2), batch, heads_q,
+                                heads_kv, batch * seq_q, batch * seq_kv, 0, 0, head_dim, nullptr, nullptr, nullptr,
+                                nullptr, nullptr, nullptr, nullptr, nullptr, 0))
+    return rc;
   if (int rc = check_arch()) return rc;
   return flash_impl(q, q_strides, k, k_strides, v, v_strides, o, o_strides, dtype, causal, batch, heads_q, heads_kv,
                     seq_q, seq_kv, head_dim, sm_scale, static_cast<cudaStream_t>(stream));
@@ -960,6 +1076,14 @@ int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dt
   const size_t need = stats + (route == Route::kCodes16 ? codes_ws_bytes(batch, heads_kv, max_seq_kv, head_dim) : 0);
   if (need && (!workspace || workspace_bytes < need))
     return fail(SAGE_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (int rc = check_attn_alias(o, os, tensor_span(o, os, 1, heads_q, total_q, head_dim, 2), q, qs,
+                                tensor_span(q, qs, 1, heads_q, total_q, head_dim, 2),
+                                tensor_span(k, ks, 1, heads_kv, total_kv, head_dim, 2),
+                                tensor_span(v, vs, 1, heads_kv, total_kv, head_dim, 2), batch, heads_q, heads_kv,
+                                total_q, total_kv, cdiv(max_seq_q, 128), cdiv(max_seq_kv, 64), head_dim, q_i8, q_scale,
+                                k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace,
+                                workspace_bytes))
+    return rc;
   if (int rc = check_arch()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Varlen vl{cu_seqlens_q, cu_seqlens_kv, total_q, total_kv};
@@ -995,6 +1119,13 @@ int sage_flash_attn_varlen_fwd(const void* q, const void* k, const void* v, void
   if (!q || !k || !v || !o) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/v/o must be 16-byte aligned");
+  if (int rc = check_attn_alias(o, os, tensor_span(o, os, 1, heads_q, total_q, head_dim, 2), q, qs,
+                                tensor_span(q, qs, 1, heads_q, total_q, head_dim, 2),
+                                tensor_span(k, ks, 1, heads_kv, total_kv, head_dim, 2),
+                                tensor_span(v, vs, 1, heads_kv, total_kv, head_dim, 2), batch, heads_q, heads_kv,
+                                total_q, total_kv, 0, 0, head_dim, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                nullptr, nullptr, 0))
+    return rc;
   if (int rc = check_arch()) return rc;
   const Varlen vl{cu_seqlens_q, cu_seqlens_kv, total_q, total_kv};
   return flash_impl(q, qs, k, ks, v, vs, o, os, dtype, causal, batch, heads_q, heads_kv, max_seq_q, max_seq_kv,
