@@ -17,7 +17,9 @@ Cases (all [B, H, S, D], HND layout):
   ties     B1 H1 S64 D64   fp16 K block whose absmax is 127, so x/scale hits .5 exactly
   zeroblk  B1 H1 S192 D64  fp16 with the first 128-row Q block all zero (scale 0)
 For every case the fixture holds q/k/v, the reference quantisation without smoothing
-(q_i8, q_scale, k_i8, k_scale), the smoothed K quantisation through the reference's own
+(q_i8, q_scale, k_i8, k_scale), the reference's Q quantisation with finer blocks through its
+own BLKQ argument (q_i8_b{1,16,32,64}, q_scale_b{1,16,32,64}; triton_impl.py:35, 57, 63), the
+smoothed K quantisation through the reference's own
 ``km`` argument with the oracle's fp32 channel mean (km, k_i8_sm, k_scale_sm), the reference
 Triton output (o_triton, non-causal cases) and the fp32 exact output of ``ref`` (o_ref).
 """
@@ -57,6 +59,10 @@ def run_case(name, q, k, v, dtype, causal=False):
     kt = torch.tensor(k, dtype=torch.float32).to(tdt)
     vt = torch.tensor(v, dtype=torch.float32).to(tdt)
     q_i8, q_scale, k_i8, k_scale = triton_impl.per_block_int8(qt, kt, BLKQ=128, BLKK=64)
+    fine = {}
+    for blkq in (1, 16, 32, 64):
+        qb, qsb, _, _ = triton_impl.per_block_int8(qt, kt, BLKQ=blkq, BLKK=64)
+        fine[f"q_i8_b{blkq}"], fine[f"q_scale_b{blkq}"] = qb.numpy(), qsb.numpy()
     km = oracle.k_mean(kt.float().numpy())  # [B, Hkv, D] fp32
     kmt = torch.tensor(km).unsqueeze(2)  # [B, Hkv, 1, D] fp32 -> k - km evaluated in fp32
     _, _, k_i8_sm, k_scale_sm = triton_impl.per_block_int8(qt, kt, km=kmt, BLKQ=128, BLKK=64)
@@ -72,6 +78,7 @@ def run_case(name, q, k, v, dtype, causal=False):
         "k_i8_sm": k_i8_sm.numpy(),
         "k_scale_sm": k_scale_sm.numpy(),
         "meta": np.array([1 if dtype == "bf16" else 0, 1 if causal else 0], dtype=np.int32),
+        **fine,
     }
     if not causal:
         o_tri = triton_impl.run_sage_attn(qt, kt, vt).float().numpy()

@@ -34,6 +34,18 @@ def test_quant_bit_exact_vs_reference(golden, case):
 
 
 @pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("blkq", [1, 16, 32, 64])
+def test_fine_q_blocks_bit_exact_vs_reference(golden, case, blkq):
+    """The reference's BLKQ argument (triton_impl.py:35, 57, 63): Q blocks of 64, 32, 16 rows and
+    one row (per token) quantised by the reference itself equal the oracle bit for bit."""
+    q = _f32(golden(case, "q"))
+    qi, qs = oracle.quant_per_block_int8(q, blkq, oracle.q_multiplier(None, q.shape[-1]))
+    assert qs.shape[-1] == -(-q.shape[2] // blkq)
+    np.testing.assert_array_equal(qi, golden(case, f"q_i8_b{blkq}"))
+    np.testing.assert_array_equal(qs, golden(case, f"q_scale_b{blkq}"))
+
+
+@pytest.mark.parametrize("case", CASES)
 def test_smoothed_quant_bit_exact_vs_reference_km(golden, case):
     """The reference's own smoothing path (per_block_int8(..., km=<fp32 km>)) equals the oracle."""
     k = _f32(golden(case, "k"))
