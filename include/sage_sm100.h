@@ -15,8 +15,9 @@
  *   head_dim must be 64 or 128.
  *
  * Quantised intermediates, all owned by the caller and always contiguous:
- *   q_i8    int8  [B, Hq,  Sq,  D]      per-128-row-block INT8 Q (sm_scale*log2(e) folded in)
- *   q_scale fp32  [B, Hq,  ceil(Sq/128)]
+ *   q_i8    int8  [B, Hq,  Sq,  D]      per-block INT8 Q (sm_scale*log2(e) folded in), blocks of
+ *                                       BLKQ = 128 rows unless SAGE_FLAG_QBLK_* says otherwise
+ *   q_scale fp32  [B, Hq,  ceil(Sq/BLKQ)]
  *   k_i8    int8  [B, Hkv, Skv, D]      per-64-row-block INT8 K (after optional smoothing)
  *   k_scale fp32  [B, Hkv, ceil(Skv/64)]
  *   k_mean  fp32  [B, Hkv, D]           per-channel token mean of K (smoothing only)
@@ -39,7 +40,7 @@
 extern "C" {
 #endif
 
-#define SAGE_ABI_VERSION 1
+#define SAGE_ABI_VERSION 2
 
 /* Status codes. 0 is success; everything else is negative. */
 #define SAGE_OK                    0
@@ -73,6 +74,20 @@ extern "C" {
 #define SAGE_FLAG_CODES16  16u /* sage_prepass only, head_dim 64: q_i8 / k_i8 receive the codes
                                   as fp16 values (2 bytes each: buffers of twice the size, same
                                   layouts), for sage_attn_fwd_codes16 */
+
+/* Q scale block size: per_block_int8's BLKQ argument (kernels/sage_attn/triton_impl.py:35, 57,
+ * 63), a 3-bit field of `flags`. One fp32 scale per BLKQ query rows: q_scale is
+ * [B, Hq, ceil(Sq / BLKQ)]. The default, 128 rows, is the reference's default and the one its
+ * attention kernel assumes (run_sage_attn, triton_impl.py:166); the finer blocks trade nothing
+ * in the attention kernel (each softmax thread owns one query row and reads that row's scale)
+ * for smaller INT8 rounding errors on rows with outliers. The attention entry points take the
+ * same field, so that they read the scales the pre-pass wrote. */
+#define SAGE_FLAG_QBLK_MASK 0x700u
+#define SAGE_FLAG_QBLK_128  0x000u  /* 128-row blocks (default) */
+#define SAGE_FLAG_QBLK_64   0x100u
+#define SAGE_FLAG_QBLK_32   0x200u
+#define SAGE_FLAG_QBLK_16   0x300u
+#define SAGE_FLAG_QBLK_1    0x400u  /* one scale per token */
 
 /* Device-side status bits reported by sage_device_status(). */
 #define SAGE_DEV_TIMEOUT_PRODUCER 0x1
@@ -159,11 +174,13 @@ int sage_quant_v_fp8(const void* v, int dtype, int64_t batch, int64_t heads_kv, 
  * like reference.py:19-22). v is the 16-bit V ({batch, head, seq} strides v_strides)
  * for SAGE_PV_16BIT, or v_fp8 (contiguous) with v_scale for SAGE_PV_FP8.
  * GQA: heads_q % heads_kv == 0, query head h reads KV head h / (heads_q / heads_kv).
+ * flags: only the SAGE_FLAG_QBLK_* field (the Q scale block size q_scale was written with);
+ * any other bit is rejected. (ABI version 2 added this argument.)
  */
 int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
                   const float* k_scale, const void* v, const int64_t v_strides[3],
                   const float* v_scale, void* o, const int64_t o_strides[3],
-                  int dtype, int pv_mode, int causal,
+                  int dtype, int pv_mode, int causal, unsigned flags,
                   int64_t batch, int64_t heads_q, int64_t heads_kv,
                   int64_t seq_q, int64_t seq_kv, int64_t head_dim, void* stream);
 
@@ -173,12 +190,13 @@ int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
  * (every partial sum is an integer below 2^24), with no int32 -> float step in the softmax.
  * q_c16 [B, Hq, Sq, 64] and k_c16 [B, Hkv, Skv, 64] contiguous fp16. This is the second half of
  * sage_run at head_dim 64 (which keeps the Q codes in o and the K codes in its workspace).
+ * flags: the SAGE_FLAG_QBLK_* field only, as for sage_attn_fwd.
  */
 int sage_attn_fwd_codes16(const void* q_c16, const float* q_scale, const void* k_c16, const float* k_scale,
                           const void* v, const int64_t v_strides[3], const float* v_scale, void* o,
-                          const int64_t o_strides[3], int dtype, int pv_mode, int causal, int64_t batch,
-                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
-                          void* stream);
+                          const int64_t o_strides[3], int dtype, int pv_mode, int causal, unsigned flags,
+                          int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
+                          int64_t head_dim, void* stream);
 
 /*
  * sage_attn_fwd with the Q quantisation inside the kernel: each CTA's softmax warps load their
@@ -187,13 +205,16 @@ int sage_attn_fwd_codes16(const void* q_c16, const float* q_scale, const void* k
  * head_dim^-0.5) straight into shared memory, and attend. q_i8_out / q_scale_out, both NULL or
  * both set, receive the codes and scales in sage_per_block_int8's layouts. This is the second
  * half of sage_run at head_dim 128 (its first half: sage_prepass with SAGE_FLAG_FUSED_Q).
+ * flags: the SAGE_FLAG_QBLK_* field only: the Q blocks quantised here (finer blocks are reduced
+ * over the rows of each block inside the 128-row tile; codes and scales bit-identical to
+ * sage_per_block_int8 with the same field).
  * Replaces per_block_int8's Q half + the _attn_fwd launch (triton_impl.py:62-72, 121-160).
  */
 int sage_attn_fwd_fused_q(const void* q, const int64_t q_strides[3], float sm_scale, const int8_t* k_i8,
                           const float* k_scale, const void* v, const int64_t v_strides[3], const float* v_scale,
-                          void* o, const int64_t o_strides[3], int dtype, int pv_mode, int causal, int64_t batch,
-                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
-                          int8_t* q_i8_out, float* q_scale_out, void* stream);
+                          void* o, const int64_t o_strides[3], int dtype, int pv_mode, int causal,
+                          unsigned flags, int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
+                          int64_t seq_kv, int64_t head_dim, int8_t* q_i8_out, float* q_scale_out, void* stream);
 
 /*
  * The pre-pass half of sage_run on its own: K smoothing statistics, INT8 Q/K and (for

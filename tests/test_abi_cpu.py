@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert N.load().sage_abi_version() == N.SAGE_ABI_VERSION == 1
+    assert N.load().sage_abi_version() == N.SAGE_ABI_VERSION == 2
 
 
 def test_workspace_bytes():
@@ -83,12 +83,12 @@ def test_attn_rejects_causal_with_unequal_lengths_and_bad_mode():
     lib = N.load()
     keep, p = _dummy()
     s = N.strides3(8 * 128, 8 * 128, 128)
-    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 1, 1, 1, 1, 8, 16, 128,
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 1, 0, 1, 1, 1, 8, 16, 128,
                            None)
     assert rc == N.SAGE_ERR_INVALID_ARG and "causal" in lib.sage_last_error().decode()
-    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, 7, 0, 1, 1, 1, 8, 8, 128, None)
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, 7, 0, 0, 1, 1, 1, 8, 8, 128, None)
     assert rc == N.SAGE_ERR_INVALID_ARG
-    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, 5, N.SAGE_PV_16BIT, 0, 1, 1, 1, 8, 8, 128, None)
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, 5, N.SAGE_PV_16BIT, 0, 0, 1, 1, 1, 8, 8, 128, None)
     assert rc == N.SAGE_ERR_INVALID_ARG and "dtype" in lib.sage_last_error().decode()
 
 
@@ -96,10 +96,10 @@ def test_rejects_gqa_mismatch_and_empty():
     lib = N.load()
     keep, p = _dummy()
     s = N.strides3(8 * 128, 8 * 128, 128)
-    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 1, 3, 2, 8, 8, 128,
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 0, 1, 3, 2, 8, 8, 128,
                            None)
     assert rc == N.SAGE_ERR_INVALID_ARG and "multiple" in lib.sage_last_error().decode()
-    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 1, 1, 1, 0, 8, 128,
+    rc = lib.sage_attn_fwd(p, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 0, 1, 1, 1, 0, 8, 128,
                            None)
     assert rc == N.SAGE_ERR_INVALID_ARG
 
@@ -109,7 +109,7 @@ def test_rejects_misaligned_pointer():
     keep, p = _dummy()
     bad = ctypes.c_void_p(p.value + 4)
     s = N.strides3(8 * 128, 8 * 128, 128)
-    rc = lib.sage_attn_fwd(bad, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 1, 1, 1, 8, 8, 128,
+    rc = lib.sage_attn_fwd(bad, p, p, p, p, s, None, p, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 0, 1, 1, 1, 8, 8, 128,
                            None)
     assert rc == N.SAGE_ERR_INVALID_ARG and "aligned" in lib.sage_last_error().decode()
 
@@ -218,7 +218,7 @@ def test_output_aliasing_is_rejected_before_any_cuda_call():
     assert run(off(k, 64), head_dim=64, flags=N.SAGE_FLAG_SMOOTH_K) == N.SAGE_ERR_INVALID_ARG
 
     # the split entry point and the flash pack check the same way
-    rc = lib.sage_attn_fwd(qi, qsc, ki, ksc, v, s, None, off(ki, 128), s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 1, 1,
+    rc = lib.sage_attn_fwd(qi, qsc, ki, ksc, v, s, None, off(ki, 128), s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, 0, 1, 1,
                            1, 8, 8, 128, None)
     assert rc == N.SAGE_ERR_INVALID_ARG and "overlaps k_i8" in msg()
     rc = lib.sage_flash_attn_fwd(q, k, v, off(v, 2032), N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 128, s, s, s, s, 0, 0.0, None)
@@ -234,3 +234,30 @@ def test_output_aliasing_is_rejected_before_any_cuda_call():
                              0, 0.0, N.SAGE_PV_16BIT, N.SAGE_FLAG_PREPASS_Q, qi, qsc, ki, ksc, None, None, None, None,
                              0, None)
     assert rc == N.SAGE_ERR_INVALID_ARG and "overlaps k" in msg()
+
+
+def test_q_block_field_is_validated():
+    """Host-side validation (no device here): a SAGE_FLAG_QBLK_* field outside the five sizes,
+    or any other flag on an attention-only entry point, is SAGE_ERR_INVALID_ARG."""
+    lib = N.load()
+    keep, (q, k, qi, qsc, ki, ksc, v, o) = _distinct(8)
+    s = N.strides3(8 * 128, 8 * 128, 128)
+
+    def pbi8(flags):
+        return lib.sage_per_block_int8(q, k, N.SAGE_DTYPE_F16, 1, 1, 1, 8, 8, 128, s, s, ctypes.c_float(0.0), flags,
+                                       qi, qsc, ki, ksc, None, None, 0, None)
+
+    for blkq, bits in N.SAGE_FLAG_QBLK.items():
+        assert pbi8(bits) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG), blkq  # valid: stops at the device
+    for bad in (0x500, 0x600, 0x700):
+        assert pbi8(bad) == N.SAGE_ERR_INVALID_ARG and "SAGE_FLAG_QBLK" in lib.sage_last_error().decode()
+
+    def attn(flags):
+        return lib.sage_attn_fwd(qi, qsc, ki, ksc, v, s, None, o, s, N.SAGE_DTYPE_F16, N.SAGE_PV_16BIT, 0, flags,
+                                 1, 1, 1, 8, 8, 128, None)
+
+    assert attn(N.SAGE_FLAG_QBLK[1]) not in (N.SAGE_OK, N.SAGE_ERR_INVALID_ARG)
+    assert attn(N.SAGE_FLAG_SMOOTH_K) == N.SAGE_ERR_INVALID_ARG
+    assert attn(0x500) == N.SAGE_ERR_INVALID_ARG
+    with pytest.raises(ValueError, match="BLKQ=8"):
+        N.qblk_flag(8)

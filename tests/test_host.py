@@ -101,9 +101,16 @@ def test_no_cpu_fallback():
 
 
 def test_per_block_int8_rejects_other_block_sizes():
+    """BLKQ takes the five sizes the kernels implement (128, 64, 32, 16, 1); BLKK only 64. Both
+    are checked before any tensor is looked at (these are CPU tensors)."""
     q = torch.randn(1, 1, 8, 64, dtype=torch.float16)
-    with pytest.raises(ValueError, match="BLKQ"):
-        tb.per_block_int8(q, q, BLKQ=64)
+    for blkq in (8, 48, 256):
+        with pytest.raises(ValueError, match="BLKQ"):
+            tb.per_block_int8(q, q, BLKQ=blkq)
+    with pytest.raises(ValueError, match="BLKK"):
+        tb.per_block_int8(q, q, BLKK=32)
+    with pytest.raises(ValueError, match="blkq|BLKQ"):
+        tb.SagePlan(1, 1, 1, 8, 8, 64, torch.float16, "cpu", blkq=3)
 
 
 def test_product_does_not_import_oracle():

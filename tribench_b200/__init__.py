@@ -1,8 +1,9 @@
 """tribench_b200 — B200-native (sm_100a) implementation of TriBench's sage_attn path.
 
 Public API (mirrors kernels/sage_attn/triton_impl.py and reference.py):
-  run / run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=True)
+  run / run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=True, blkq=128)
   per_block_int8(q, k, km=None, BLKQ=128, BLKK=64, sm_scale=None, tensor_layout="HND")
+    (BLKQ / blkq: query rows per Q scale, 128, 64, 32, 16 or 1)
   quant_v_fp8(v), attn_fwd(quant, v, causal), SagePlan (preallocated repeated calls; cuda_graph()
   captures one call for single-launch replay)
   HostPipeline (host q/k/v -> host output, PCIe copies overlapped with the computation)

@@ -18,6 +18,8 @@ ROOT_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libsage_sm100.so")
+# the tcgen05 throughput microbenchmark (include/sm100_peaks.h), a library of its own
+PEAKS_LIB_PATH = os.path.join(LIB_DIR, "libsm100_peaks.so")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -35,31 +37,50 @@ def _nvcc() -> str:
 
 
 def _sources() -> list[str]:
-    srcs = glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cuh"))
+    srcs = glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(CSRC, "sage_abi.cu")]
     srcs.append(os.path.join(ROOT_DIR, "include", "sage_sm100.h"))
     return srcs
 
 
-def is_stale() -> bool:
-    if not os.path.exists(LIB_PATH):
+def _peaks_sources() -> list[str]:
+    return [os.path.join(CSRC, "tensor_peaks.cu"), os.path.join(CSRC, "sm100_ptx.cuh"),
+            os.path.join(ROOT_DIR, "include", "sm100_peaks.h")]
+
+
+def _stale(lib: str, sources: list[str]) -> bool:
+    if not os.path.exists(lib):
         return True
-    t = os.path.getmtime(LIB_PATH)
-    return any(os.path.getmtime(s) > t for s in _sources())
+    t = os.path.getmtime(lib)
+    return any(os.path.getmtime(s) > t for s in sources)
 
 
-def build_library(force: bool = False, verbose: bool = False) -> str:
-    if not force and not is_stale():
-        return LIB_PATH
+def is_stale() -> bool:
+    return _stale(LIB_PATH, _sources())
+
+
+def _compile(source: str, lib: str, verbose: bool) -> None:
     os.makedirs(LIB_DIR, exist_ok=True)
-    tmp = LIB_PATH + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, "-o", tmp, os.path.join(CSRC, "sage_abi.cu")]
+    tmp = lib + ".tmp"
+    cmd = [_nvcc(), *NVCC_FLAGS, "-o", tmp, source]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB_PATH)
+    os.replace(tmp, lib)
+
+
+def build_library(force: bool = False, verbose: bool = False) -> str:
+    if force or is_stale():
+        _compile(os.path.join(CSRC, "sage_abi.cu"), LIB_PATH, verbose)
     return LIB_PATH
+
+
+def build_peaks_library(force: bool = False, verbose: bool = False) -> str:
+    if force or _stale(PEAKS_LIB_PATH, _peaks_sources()):
+        _compile(os.path.join(CSRC, "tensor_peaks.cu"), PEAKS_LIB_PATH, verbose)
+    return PEAKS_LIB_PATH
 
 
 if __name__ == "__main__":
     print(build_library(force=True, verbose="-v" in sys.argv))
+    print(build_peaks_library(force=True, verbose="-v" in sys.argv))

@@ -11,7 +11,7 @@ import threading
 from ._build import LIB_PATH
 
 # Constants mirrored from include/sage_sm100.h.
-SAGE_ABI_VERSION = 1
+SAGE_ABI_VERSION = 2
 SAGE_OK = 0
 SAGE_ERR_INVALID_ARG = -1
 SAGE_ERR_UNSUPPORTED_ARCH = -2
@@ -27,6 +27,16 @@ SAGE_FLAG_KM_GIVEN = 2
 SAGE_FLAG_FUSED_Q = 4
 SAGE_FLAG_PREPASS_Q = 8
 SAGE_FLAG_CODES16 = 16
+# Q scale block size field (per_block_int8's BLKQ)
+SAGE_FLAG_QBLK_MASK = 0x700
+SAGE_FLAG_QBLK = {128: 0x000, 64: 0x100, 32: 0x200, 16: 0x300, 1: 0x400}
+
+
+def qblk_flag(blkq: int) -> int:
+    """SAGE_FLAG_QBLK_* bits for a Q block of `blkq` rows (128, 64, 32, 16 or 1)."""
+    if blkq not in SAGE_FLAG_QBLK:
+        raise ValueError(f"BLKQ={blkq} unsupported: the sm_100a kernels take Q blocks of 128, 64, 32, 16 or 1 rows")
+    return SAGE_FLAG_QBLK[blkq]
 
 # Every symbol the header declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -45,11 +55,11 @@ SIGNATURES = {
     "sage_per_block_int8_noalloc": (_I, [_P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _F, _U,
                                          _P, _P, _P, _P, _P, _P]),
     "sage_quant_v_fp8": (_I, [_P, _I, _I64, _I64, _I64, _I64, _I64P, _P, _P, _P, _SZ, _P]),
-    "sage_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I,
+    "sage_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I, _U,
                            _I64, _I64, _I64, _I64, _I64, _I64, _P]),
-    "sage_attn_fwd_codes16": (_I, [_P, _P, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I,
+    "sage_attn_fwd_codes16": (_I, [_P, _P, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I, _U,
                                    _I64, _I64, _I64, _I64, _I64, _I64, _P]),
-    "sage_attn_fwd_fused_q": (_I, [_P, _I64P, _F, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I,
+    "sage_attn_fwd_fused_q": (_I, [_P, _I64P, _F, _P, _P, _P, _I64P, _P, _P, _I64P, _I, _I, _I, _U,
                                    _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "sage_prepass": (_I, [_P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _F, _I, _U,
                           _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),

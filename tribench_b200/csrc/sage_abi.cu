@@ -117,6 +117,28 @@ int check_shape(int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Rows per Q scale block from the SAGE_FLAG_QBLK_* field of `flags` (per_block_int8's BLKQ).
+int qblk_from_flags(unsigned flags, int* rows) {
+  static const int kRows[8] = {128, 64, 32, 16, 1, 0, 0, 0};
+  *rows = kRows[(flags & SAGE_FLAG_QBLK_MASK) >> 8];
+  if (!*rows) return fail(SAGE_ERR_INVALID_ARG, "Q block field 0x%x of flags is not a SAGE_FLAG_QBLK_* value",
+                          flags & SAGE_FLAG_QBLK_MASK);
+  return SAGE_OK;
+}
+int qblk_shift(int rows) { return rows == 1 ? 0 : rows == 16 ? 4 : rows == 32 ? 5 : rows == 64 ? 6 : 7; }
+// Rows per Q block of flags that passed qblk_from_flags.
+int qblk_of(unsigned flags) {
+  int rows = 128;
+  qblk_from_flags(flags, &rows);
+  return rows;
+}
+// The attention-only entry points take the Q block field and nothing else.
+int check_attn_flags(unsigned flags, int* rows) {
+  if (flags & ~SAGE_FLAG_QBLK_MASK)
+    return fail(SAGE_ERR_INVALID_ARG, "flags 0x%x: the attention entry points take only SAGE_FLAG_QBLK_*", flags);
+  return qblk_from_flags(flags, rows);
+}
+
 // ---------------------------------------------------------------- output aliasing
 // Byte range [lo, hi) a buffer covers. A strided [B, H, S, D] tensor (element strides {batch,
 // head, seq}, D contiguous) covers everything between its first and its last element.
@@ -296,12 +318,27 @@ void launch_qquant_kernel(const sage::PrepassParams& p, bool packed, bool c16, c
   }
 }
 
+// Q quantisation with blocks finer than 128 rows (SAGE_FLAG_QBLK_*): one 128-row CTA each.
+template <int D, typename T>
+void launch_qquant_fine_kernel(const sage::PrepassParams& p, bool packed, bool c16, cudaStream_t st) {
+  const dim3 g((unsigned)p.n_q);
+  if constexpr (D == 64) {
+    if (c16) {
+      if (packed) sage::qquant_fine_kernel<D, T, true, true><<<g, sage::kKQuantThreads, 0, st>>>(p);
+      else sage::qquant_fine_kernel<D, T, false, true><<<g, sage::kKQuantThreads, 0, st>>>(p);
+      return;
+    }
+  }
+  if (packed) sage::qquant_fine_kernel<D, T, true, false><<<g, sage::kKQuantThreads, 0, st>>>(p);
+  else sage::qquant_fine_kernel<D, T, false, false><<<g, sage::kKQuantThreads, 0, st>>>(p);
+}
+
 template <int D, typename T>
 int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                    int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs, float q_mult, bool smooth,
                    bool km_given, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale, float* k_mean,
                    uint8_t* v_fp8, float* v_scale, void* ws, const Varlen* vl, const Codes16* c16,
-                   cudaStream_t st) {
+                   cudaStream_t st, int qblk) {
   const int nchunk = static_cast<int>(cdiv(Skv, sage::kStatsChunk));
   const bool want_v = v_fp8 != nullptr;
   const bool want_km = smooth && !km_given && k != nullptr;
@@ -321,7 +358,8 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
     p.q_c16 = c16->q; p.k_c16 = c16->k;
     if (c16->qs) { p.qc_sb = vl ? 0 : c16->qs[0]; p.qc_sh = c16->qs[1]; p.qc_ss = c16->qs[2]; }
   }
-  p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, sage::kVRowsPerCta<D>); p.nchunk = nchunk;
+  p.qblk = qblk;
+  p.nqb = (int)cdiv(Sq, qblk); p.nkb = (int)cdiv(Skv, 64); p.nvb = (int)cdiv(Skv, sage::kVRowsPerCta<D>); p.nchunk = nchunk;
   const int64_t n_q = q ? B * Hq * cdiv(p.nqb, sage::kQBlocksPerCta<D>) : 0;
   const int64_t n_k = k ? B * Hkv * cdiv(p.nkb, sage::kKBlocksPerCta<D>) : 0;
   const int64_t n_v = want_v ? B * Hkv * p.nvb : 0;
@@ -335,11 +373,20 @@ int launch_prepass(const void* q, const void* k, const void* v, int64_t B, int64
     p.stat_k = want_km ? 1 : 0;
     p.stat_v = want_v ? 1 : 0;
   }
+  // Q blocks finer than 128 rows: their own 128-thread launch (qquant_fine_kernel) at either
+  // head_dim, before the statistics
+  bool q_done = false;
+  if (n_q > 0 && qblk != 128) {
+    p.n_q = (int)(B * Hq * cdiv(Sq, 128));
+    p.n_stat = p.n_k = p.n_v = 0;
+    launch_qquant_fine_kernel<D, T>(p, vl != nullptr, c16 != nullptr, st);
+    SAGE_CUDA_TRY(cudaGetLastError());
+    q_done = true;
+  }
   // Q blocks at head_dim 64 in their own 128-thread launch (every Q block the pre-pass sees at
   // 64: the fp16-code and INT8 routes)
-  bool q_done = false;
   if constexpr (D == 64) {
-    if (n_q > 0) {
+    if (n_q > 0 && !q_done) {
       p.n_q = (int)(B * Hq * p.nqb);
       p.n_stat = p.n_k = p.n_v = 0;
       launch_qquant_kernel<T>(p, vl != nullptr, c16 != nullptr, st);
@@ -400,19 +447,19 @@ int prepass_dispatch(int dtype, int64_t D, const void* q, const void* k, const v
                      int64_t Hkv, int64_t Sq, int64_t Skv, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                      float q_mult, bool smooth, bool km_given, int8_t* q_i8, float* q_scale, int8_t* k_i8, float* k_scale,
                      float* k_mean, uint8_t* v_fp8, float* v_scale, void* ws, cudaStream_t st,
-                     const Varlen* vl = nullptr, const Codes16* c16 = nullptr) {
+                     const Varlen* vl = nullptr, const Codes16* c16 = nullptr, int qblk = 128) {
   if (dtype == SAGE_DTYPE_F16) {
     if (D == 128)
       return launch_prepass<128, __half>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale, k_i8,
-                                         k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st);
+                                         k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st, qblk);
     return launch_prepass<64, __half>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale, k_i8,
-                                      k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st);
+                                      k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st, qblk);
   }
   if (D == 128)
     return launch_prepass<128, __nv_bfloat16>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale,
-                                              k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st);
+                                              k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st, qblk);
   return launch_prepass<64, __nv_bfloat16>(q, k, v, B, Hq, Hkv, Sq, Skv, qs, ks, vs, q_mult, smooth, km_given, q_i8, q_scale,
-                                           k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st);
+                                           k_i8, k_scale, k_mean, v_fp8, v_scale, ws, vl, c16, st, qblk);
 }
 
 // ---------------------------------------------------------------- attention launch
@@ -441,6 +488,7 @@ void set_seq_params(sage::AttnParams& p, const Varlen* vl, const int64_t* os, in
   p.B = (int)B; p.Hq = (int)Hq; p.Hkv = (int)Hkv; p.Sq = (int)Sq; p.Skv = (int)Skv;
   p.groups = (int)(Hq / Hkv);
   p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64);
+  p.qblk_shift = 7;
   p.causal = causal ? 1 : 0;
   p.n_m_ctas = (int)cdiv(Sq, 256);
   p.wait_limit_ns = wait_limit_ns();
@@ -485,7 +533,8 @@ struct FusedQ {
 int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale, const void* v,
               const int64_t* vs, const float* v_scale, void* o, const int64_t* os, int dtype, int pv_mode, int causal,
               int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, cudaStream_t st,
-              const Varlen* vl = nullptr, const FusedQ* fq = nullptr, const Codes16* c16 = nullptr) {
+              const Varlen* vl = nullptr, const FusedQ* fq = nullptr, const Codes16* c16 = nullptr,
+              int qblk = 128) {
   const bool fp8 = pv_mode == SAGE_PV_FP8;
   // rows of the token axis and batch extent of every tensor map (packed sequences: one batch)
   const int64_t rq = vl ? vl->q_tokens : Sq, rk = vl ? vl->k_tokens : Skv, nb = vl ? 1 : B;
@@ -524,6 +573,8 @@ int attn_impl(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, cons
   sage::AttnParams p{};
   p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.o = o;
   set_seq_params(p, vl, os, B, Hq, Hkv, Sq, Skv, causal);
+  p.qblk_shift = qblk_shift(qblk);
+  p.nqb = (int)cdiv(Sq, qblk);
   if (fq) {
     p.q_src = fq->q;
     p.q_sb = vl ? 0 : fq->qs[0]; p.q_sh = fq->qs[1]; p.q_ss = fq->qs[2];
@@ -635,6 +686,8 @@ int sage_per_block_int8(const void* q, const void* k, int dtype, int64_t batch, 
   if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
   if (int rc = check_strides("q", q_strides)) return rc;
   if (int rc = check_strides("k", k_strides)) return rc;
+  int qblk = 128;
+  if (int rc = qblk_from_flags(flags, &qblk)) return rc;
   if (!q || !k || !q_i8 || !q_scale || !k_i8 || !k_scale) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(q_i8) || !aligned16(k_i8))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/q_i8/k_i8 must be 16-byte aligned");
@@ -647,7 +700,8 @@ int sage_per_block_int8(const void* q, const void* k, int dtype, int64_t batch, 
   if (int rc = check_arch()) return rc;
   return prepass_dispatch(dtype, head_dim, q, k, nullptr, batch, heads_q, heads_kv, seq_q, seq_kv, q_strides,
                           k_strides, nullptr, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8, q_scale, k_i8,
-                          k_scale, k_mean, nullptr, nullptr, workspace, static_cast<cudaStream_t>(stream));
+                          k_scale, k_mean, nullptr, nullptr, workspace, static_cast<cudaStream_t>(stream), nullptr,
+                          nullptr, qblk);
 }
 
 int sage_per_block_int8_noalloc(const void* q, const void* k, int dtype, int64_t batch, int64_t heads_q,
@@ -659,6 +713,8 @@ int sage_per_block_int8_noalloc(const void* q, const void* k, int dtype, int64_t
   if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
   if (int rc = check_strides("q", q_strides)) return rc;
   if (int rc = check_strides("k", k_strides)) return rc;
+  int qblk = 128;
+  if (int rc = qblk_from_flags(flags, &qblk)) return rc;
   if (!q || !k || !q_i8 || !q_scale || !k_i8 || !k_scale) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(q_i8) || !aligned16(k_i8))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/q_i8/k_i8 must be 16-byte aligned");
@@ -678,7 +734,8 @@ int sage_per_block_int8_noalloc(const void* q, const void* k, int dtype, int64_t
   }
   return prepass_dispatch(dtype, head_dim, q, k, nullptr, batch, heads_q, heads_kv, seq_q, seq_kv, q_strides,
                           k_strides, nullptr, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8, q_scale, k_i8,
-                          k_scale, k_mean, nullptr, nullptr, scratch, static_cast<cudaStream_t>(stream));
+                          k_scale, k_mean, nullptr, nullptr, scratch, static_cast<cudaStream_t>(stream), nullptr,
+                          nullptr, qblk);
 }
 
 int sage_quant_v_fp8(const void* v, int dtype, int64_t batch, int64_t heads_kv, int64_t seq_kv, int64_t head_dim,
@@ -700,10 +757,12 @@ int sage_quant_v_fp8(const void* v, int dtype, int64_t batch, int64_t heads_kv, 
 
 int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale, const void* v,
                   const int64_t v_strides[3], const float* v_scale, void* o, const int64_t o_strides[3], int dtype,
-                  int pv_mode, int causal, int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
-                  int64_t seq_kv, int64_t head_dim, void* stream) {
+                  int pv_mode, int causal, unsigned flags, int64_t batch, int64_t heads_q, int64_t heads_kv,
+                  int64_t seq_q, int64_t seq_kv, int64_t head_dim, void* stream) {
   g_last_error.clear();
   if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  int qblk = 128;
+  if (int rc = check_attn_flags(flags, &qblk)) return rc;
   if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
   if (causal && seq_q != seq_kv)
@@ -724,22 +783,25 @@ int sage_attn_fwd(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, 
                          : tensor_span(v, v_strides, batch, heads_kv, seq_kv, head_dim, 2);
     if (int rc = check_attn_alias(o, o_strides, tensor_span(o, o_strides, batch, heads_q, seq_q, head_dim, 2), nullptr,
                                   nullptr, Span{}, Span{}, vsp, batch, heads_q, heads_kv, batch * seq_q, batch * seq_kv,
-                                  cdiv(seq_q, 128), cdiv(seq_kv, 64), head_dim, q_i8, q_scale, k_i8, k_scale, nullptr,
+                                  cdiv(seq_q, qblk), cdiv(seq_kv, 64), head_dim, q_i8, q_scale, k_i8, k_scale, nullptr,
                                   nullptr, fp8 ? v_scale : nullptr, nullptr, 0))
       return rc;
   }
   if (int rc = check_arch()) return rc;
   return attn_impl(q_i8, q_scale, k_i8, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal, batch,
-                   heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream));
+                   heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream), nullptr, nullptr,
+                   nullptr, qblk);
 }
 
 int sage_attn_fwd_fused_q(const void* q, const int64_t q_strides[3], float sm_scale, const int8_t* k_i8,
                           const float* k_scale, const void* v, const int64_t v_strides[3], const float* v_scale,
-                          void* o, const int64_t o_strides[3], int dtype, int pv_mode, int causal, int64_t batch,
-                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
-                          int8_t* q_i8_out, float* q_scale_out, void* stream) {
+                          void* o, const int64_t o_strides[3], int dtype, int pv_mode, int causal,
+                          unsigned flags, int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
+                          int64_t seq_kv, int64_t head_dim, int8_t* q_i8_out, float* q_scale_out, void* stream) {
   g_last_error.clear();
   if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  int qblk = 128;
+  if (int rc = check_attn_flags(flags, &qblk)) return rc;
   if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
   if (causal && seq_q != seq_kv)
@@ -762,7 +824,7 @@ int sage_attn_fwd_fused_q(const void* q, const int64_t q_strides[3], float sm_sc
                          : tensor_span(v, v_strides, batch, heads_kv, seq_kv, head_dim, 2);
     if (int rc = check_attn_alias(o, o_strides, tensor_span(o, o_strides, batch, heads_q, seq_q, head_dim, 2), q,
                                   q_strides, tensor_span(q, q_strides, batch, heads_q, seq_q, head_dim, 2), Span{}, vsp,
-                                  batch, heads_q, heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, 128),
+                                  batch, heads_q, heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, qblk),
                                   cdiv(seq_kv, 64), head_dim, q_i8_out, q_scale_out, k_i8, k_scale, nullptr, nullptr,
                                   fp8 ? v_scale : nullptr, nullptr, 0))
       return rc;
@@ -770,16 +832,19 @@ int sage_attn_fwd_fused_q(const void* q, const int64_t q_strides[3], float sm_sc
   if (int rc = check_arch()) return rc;
   const FusedQ fq{q, q_strides, q_multiplier(sm_scale, head_dim), q_i8_out, q_scale_out};
   return attn_impl(nullptr, nullptr, k_i8, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal,
-                   batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream), nullptr, &fq);
+                   batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream), nullptr, &fq,
+                   nullptr, qblk);
 }
 
 int sage_attn_fwd_codes16(const void* q_c16, const float* q_scale, const void* k_c16, const float* k_scale,
                           const void* v, const int64_t v_strides[3], const float* v_scale, void* o,
-                          const int64_t o_strides[3], int dtype, int pv_mode, int causal, int64_t batch,
-                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
-                          void* stream) {
+                          const int64_t o_strides[3], int dtype, int pv_mode, int causal, unsigned flags,
+                          int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
+                          int64_t head_dim, void* stream) {
   g_last_error.clear();
   if (int rc = check_shape(dtype, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)) return rc;
+  int qblk = 128;
+  if (int rc = check_attn_flags(flags, &qblk)) return rc;
   if (head_dim != 64) return fail(SAGE_ERR_INVALID_ARG, "fp16 codes are the head_dim-64 route");
   if (pv_mode != SAGE_PV_16BIT && pv_mode != SAGE_PV_FP8)
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
@@ -804,7 +869,7 @@ int sage_attn_fwd_codes16(const void* q_c16, const float* q_scale, const void* k
     const Span ksp = buffer_span(k_c16, static_cast<size_t>(batch * heads_kv * seq_kv * head_dim) * 2);
     if (int rc = check_attn_alias(o, o_strides, tensor_span(o, o_strides, batch, heads_q, seq_q, head_dim, 2), q_c16,
                                   qcs, tensor_span(q_c16, qcs, batch, heads_q, seq_q, head_dim, 2), ksp, vsp, batch,
-                                  heads_q, heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, 128), cdiv(seq_kv, 64),
+                                  heads_q, heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, qblk), cdiv(seq_kv, 64),
                                   head_dim, nullptr, q_scale, nullptr, k_scale, nullptr, nullptr,
                                   fp8 ? v_scale : nullptr, nullptr, 0))
       return rc;
@@ -814,7 +879,7 @@ int sage_attn_fwd_codes16(const void* q_c16, const float* q_scale, const void* k
                     static_cast<__half*>(const_cast<void*>(k_c16))};
   return attn_impl(nullptr, q_scale, nullptr, k_scale, v, v_strides, v_scale, o, o_strides, dtype, pv_mode, causal,
                    batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, static_cast<cudaStream_t>(stream), nullptr,
-                   nullptr, &c16);
+                   nullptr, &c16, qblk);
 }
 
 namespace {
@@ -846,6 +911,8 @@ int check_run_args(const void* q, const void* k, const void* v, int dtype, int64
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
   if ((flags & SAGE_FLAG_FUSED_Q) && (flags & SAGE_FLAG_PREPASS_Q))
     return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_FUSED_Q and SAGE_FLAG_PREPASS_Q exclude each other");
+  int qblk = 128;
+  if (int rc = qblk_from_flags(flags, &qblk)) return rc;
   if (int rc = check_strides("q", q_strides)) return rc;
   if (int rc = check_strides("k", k_strides)) return rc;
   if (int rc = check_strides("v", v_strides)) return rc;
@@ -894,7 +961,7 @@ int sage_prepass(const void* q, const void* k, const void* v, int dtype, int64_t
                           smooth && (flags & SAGE_FLAG_KM_GIVEN) != 0, fused_q ? nullptr : q_i8,
                           fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr,
                           fp8 ? v_scale : nullptr, workspace, static_cast<cudaStream_t>(stream), nullptr,
-                          codes16 ? &c16 : nullptr);
+                          codes16 ? &c16 : nullptr, qblk_of(flags));
 }
 
 int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch, int64_t heads_q,
@@ -918,7 +985,8 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
                                 q_strides, tensor_span(q, q_strides, batch, heads_q, seq_q, head_dim, 2),
                                 tensor_span(k, k_strides, batch, heads_kv, seq_kv, head_dim, 2),
                                 tensor_span(v, v_strides, batch, heads_kv, seq_kv, head_dim, 2), batch, heads_q,
-                                heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, 128), cdiv(seq_kv, 64), head_dim,
+                                heads_kv, batch * seq_q, batch * seq_kv, cdiv(seq_q, qblk_of(flags)), cdiv(seq_kv, 64),
+                                head_dim,
                                 q_i8, q_scale, k_i8, k_scale, k_mean, pv_mode == SAGE_PV_FP8 ? v_fp8 : nullptr,
                                 pv_mode == SAGE_PV_FP8 ? v_scale : nullptr, workspace, workspace_bytes))
     return rc;
@@ -942,12 +1010,13 @@ int sage_run(const void* q, const void* k, const void* v, void* o, int dtype, in
   if (int rc = prepass_dispatch(dtype, head_dim, fused_q ? nullptr : q, k, fp8 ? v : nullptr, batch, heads_q,
                                 heads_kv, seq_q, seq_kv, q_strides, k_strides, v_strides, q_mult, smooth, km_given,
                                 fused_q ? nullptr : q_i8, fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean,
-                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st, nullptr, cp))
+                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st, nullptr, cp,
+                                qblk_of(flags)))
     return rc;
   const FusedQ fq{q, q_strides, q_mult, q_i8, q_scale};
   return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, v_strides,
                    fp8 ? v_scale : nullptr, o, o_strides, dtype, pv_mode, causal, batch, heads_q, heads_kv, seq_q,
-                   seq_kv, head_dim, st, nullptr, fused_q ? &fq : nullptr, cp);
+                   seq_kv, head_dim, st, nullptr, fused_q ? &fq : nullptr, cp, qblk_of(flags));
 }
 
 int sage_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,
@@ -1020,6 +1089,8 @@ int sage_per_block_int8_varlen(const void* q, const void* k, int dtype, int64_t 
   int64_t qs[3], ks[3];
   if (int rc = packed_strides("q", q_strides, qs)) return rc;
   if (int rc = packed_strides("k", k_strides, ks)) return rc;
+  int qblk = 128;
+  if (int rc = qblk_from_flags(flags, &qblk)) return rc;
   if (!q || !k || !q_i8 || !q_scale || !k_i8 || !k_scale) return fail(SAGE_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(q_i8) || !aligned16(k_i8))
     return fail(SAGE_ERR_INVALID_ARG, "q/k/q_i8/k_i8 must be 16-byte aligned");
@@ -1033,7 +1104,7 @@ int sage_per_block_int8_varlen(const void* q, const void* k, int dtype, int64_t 
   const Varlen vl{cu_seqlens_q, cu_seqlens_kv, total_q, total_kv};
   return prepass_dispatch(dtype, head_dim, q, k, nullptr, batch, heads_q, heads_kv, max_seq_q, max_seq_kv, qs, ks,
                           nullptr, q_multiplier(sm_scale, head_dim), smooth, km_given, q_i8, q_scale, k_i8, k_scale,
-                          k_mean, nullptr, nullptr, workspace, static_cast<cudaStream_t>(stream), &vl);
+                          k_mean, nullptr, nullptr, workspace, static_cast<cudaStream_t>(stream), &vl, nullptr, qblk);
 }
 
 int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch, int64_t heads_q,
@@ -1056,6 +1127,8 @@ int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dt
     return fail(SAGE_ERR_INVALID_ARG, "pv_mode %d unknown", pv_mode);
   if ((flags & SAGE_FLAG_FUSED_Q) && (flags & SAGE_FLAG_PREPASS_Q))
     return fail(SAGE_ERR_INVALID_ARG, "SAGE_FLAG_FUSED_Q and SAGE_FLAG_PREPASS_Q exclude each other");
+  int qblk = 128;
+  if (int rc = qblk_from_flags(flags, &qblk)) return rc;
   const Route route = run_route(flags, head_dim);
   const bool fused_q = route == Route::kFusedQ;
   if (!q || !k || !v || !o || !k_scale || (route != Route::kCodes16 && !k_i8) ||
@@ -1080,7 +1153,7 @@ int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dt
                                 tensor_span(q, qs, 1, heads_q, total_q, head_dim, 2),
                                 tensor_span(k, ks, 1, heads_kv, total_kv, head_dim, 2),
                                 tensor_span(v, vs, 1, heads_kv, total_kv, head_dim, 2), batch, heads_q, heads_kv,
-                                total_q, total_kv, cdiv(max_seq_q, 128), cdiv(max_seq_kv, 64), head_dim, q_i8, q_scale,
+                                total_q, total_kv, cdiv(max_seq_q, qblk), cdiv(max_seq_kv, 64), head_dim, q_i8, q_scale,
                                 k_i8, k_scale, k_mean, fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace,
                                 workspace_bytes))
     return rc;
@@ -1093,12 +1166,12 @@ int sage_run_varlen(const void* q, const void* k, const void* v, void* o, int dt
   if (int rc = prepass_dispatch(dtype, head_dim, fused_q ? nullptr : q, k, fp8 ? v : nullptr, batch, heads_q,
                                 heads_kv, max_seq_q, max_seq_kv, qs, ks, vs, q_mult, smooth, km_given,
                                 fused_q ? nullptr : q_i8, fused_q ? nullptr : q_scale, k_i8, k_scale, k_mean,
-                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st, &vl, cp))
+                                fp8 ? v_fp8 : nullptr, fp8 ? v_scale : nullptr, workspace, st, &vl, cp, qblk))
     return rc;
   const FusedQ fq{q, qs, q_mult, q_i8, q_scale};
   return attn_impl(q_i8, q_scale, k_i8, k_scale, fp8 ? static_cast<const void*>(v_fp8) : v, vs,
                    fp8 ? v_scale : nullptr, o, os, dtype, pv_mode, causal, batch, heads_q, heads_kv, max_seq_q,
-                   max_seq_kv, head_dim, st, &vl, fused_q ? &fq : nullptr, cp);
+                   max_seq_kv, head_dim, st, &vl, fused_q ? &fq : nullptr, cp, qblk);
 }
 
 int sage_flash_attn_varlen_fwd(const void* q, const void* k, const void* v, void* o, int dtype, int64_t batch,

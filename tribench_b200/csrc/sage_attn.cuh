@@ -41,13 +41,17 @@ namespace sage {
 enum PvKind : int { kPvF16 = 0, kPvBF16 = 1, kPvE4M3 = 2 };
 
 struct AttnParams {
-  const float* q_scale;  // [B, Hq, nqb]
+  const float* q_scale;  // [B, Hq, nqb]: one scale per 2^qblk_shift query rows
   const float* k_scale;  // [B, Hkv, nkb]
   const float* v_scale;  // [B, Hkv, D]  (e4m3 P.V only)
   void* o;
   int64_t o_sb, o_sh, o_ss;  // output strides, elements
   int B, Hq, Hkv, Sq, Skv, groups;  // variable-length batches: Sq / Skv = longest sequence
   int nqb, nkb;
+  // Q scale blocks of 2^qblk_shift rows: 7 (128 rows, the reference's default BLKQ), 6, 5, 4, or
+  // 0 (one scale per token). Every softmax thread owns one query row, so it simply reads its
+  // own row's scale.
+  int qblk_shift;
   // Variable-length batches (nullable): sequence b owns token rows [cu_q[b], cu_q[b+1]) of Q/O
   // and [cu_k[b], cu_k[b+1]) of K/V, whose tensors have batch extent 1 and q_tokens / k_tokens
   // rows; the scales stay [B, H, nqb / nkb] per sequence.
@@ -101,7 +105,11 @@ struct AttnCfg {
   static constexpr int NUM_BARS = 1 + 3 * NS + 6 * QT;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_QRED = OFF_MISC + 16;  // fused Q quantisation: per-warp maxima
-  static constexpr int SMEM_USED = OFF_QRED + 16 * QT;
+  // fused Q quantisation with finer Q blocks: per tile, per-warp maxima of each load pass
+  // (16 passes x 4 warps) and the 128 row scales
+  static constexpr int OFF_QFINE = OFF_QRED + 16 * QT;
+  static constexpr int QFINE_BYTES = (16 * 4 + 128) * 4;
+  static constexpr int SMEM_USED = OFF_QFINE + QFINE_BYTES * QT;
   // Pad to > half of the SM's shared memory so that exactly one CTA is resident per SM:
   // each CTA allocates all 512 TMEM columns when QT == 2.
   static constexpr int SMEM_MIN = (QT == 2) ? 118 * 1024 : 0;
@@ -200,6 +208,105 @@ __device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint3
 // pre-pass's (quant_block_role in sage_quant.cuh), so codes and scale are bit-identical to it.
 // Every softmax thread arrives on bar_q after a proxy fence, so the MMA warp may read the tile.
 // Returns the tile's scale.
+// Named barrier of warpgroup t's 128 threads (ids 3 and 4; immediate ids keep the count known).
+__device__ __forceinline__ void warpgroup_sync(int t) {
+  if (t == 0) asm volatile("bar.sync 3, 128;" ::: "memory");
+  else asm volatile("bar.sync 4, 128;" ::: "memory");
+}
+
+// fused_q_tile with Q scale blocks of 2^qblk_shift < 128 rows (1 = per token, 16, 32, 64). Pass
+// i of the loads covers rows [i * RPI, (i + 1) * RPI) of the tile (RPI = 128 / (D / 8)); a row's
+// D / 8 pieces sit in consecutive lanes of one warp. Per token: the row's absmax is a shuffle
+// reduction over those lanes. Blocks of 16-64 rows (>= RPI): each pass's absmax over the
+// warpgroup, then the maximum over the passes of a block. The scales go through shared memory
+// (qfine: 64 per-warp pass maxima, then 128 row scales) to the thread that owns each row in the
+// softmax. Returns that row's scale.
+template <class C, int D, bool OBF16>
+__device__ __forceinline__ float fused_q_tile_fine(const AttnParams& p, uint8_t* qtile, float* qfine, int t, int r,
+                                                const SeqSpan& sq, int b, int h, int tile, uint64_t* bar_q,
+                                                int row_in_tile) {
+  using T = typename std::conditional<OBF16, __nv_bfloat16, __half>::type;
+  constexpr int PR = D / 8;
+  constexpr int NP = C::BM * PR / 128;
+  constexpr int RPI = 128 / PR;  // rows per load pass
+  float* wmax = qfine;           // [NP][4]
+  float* rsc = qfine + 16 * 4;   // [128]
+  const int blk_shift = p.qblk_shift;
+  const int row0 = tile * C::BM;
+  const char* base = reinterpret_cast<const char*>(p.q_src) +
+                     ((int64_t)sq.batch * p.q_sb + (int64_t)h * p.q_sh + (int64_t)(sq.base + row0) * p.q_ss) * 2;
+  uint4 raw[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int pc = i * 128 + r, row = pc / PR, c = pc % PR;
+    raw[i] = (row0 + row < sq.len) ? ldg_nc_v4(base + (int64_t)row * p.q_ss * 2 + c * 16) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float m[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) m[i] = Half8<T>::absmax(raw[i]);
+  if (blk_shift == 0) {
+#pragma unroll
+    for (int i = 0; i < NP; ++i)
+#pragma unroll
+      for (int o = PR / 2; o > 0; o >>= 1) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+  } else {
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+      if ((r & 31) == 0) wmax[i * 4 + (r >> 5)] = m[i];
+    }
+    warpgroup_sync(t);
+    const int ppb = (1 << blk_shift) / RPI;  // passes per scale block
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const int i0 = (i / ppb) * ppb;  // the block's first pass
+      float x = 0.0f;
+      for (int j = i0; j < i0 + ppb; ++j)
+        x = fmaxf(x, fmaxf(fmaxf(wmax[j * 4], wmax[j * 4 + 1]), fmaxf(wmax[j * 4 + 2], wmax[j * 4 + 3])));
+      m[i] = x;
+    }
+  }
+  float scale[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) scale[i] = __fdiv_rn(__fmul_rn(m[i], p.q_mult), 127.0f);
+  const float2 mult2 = make_float2(p.q_mult, p.q_mult);
+  int8_t* dump = nullptr;
+  if (p.q_i8_out != nullptr) {
+    const size_t first = p.cu_q ? (size_t)h * p.q_tokens + sq.base : ((size_t)b * p.Hq + h) * (size_t)sq.len;
+    dump = p.q_i8_out + (first + row0) * D;
+  }
+  const size_t scale_head = ((size_t)b * p.Hq + h) * p.nqb;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int pc = i * 128 + r, row = pc / PR, c = pc % PR;
+    const float rcp = __frcp_rn(scale[i]);
+    const float2 s2 = make_float2(scale[i], scale[i]), ns2 = make_float2(-scale[i], -scale[i]);
+    const float2 r2 = make_float2(rcp, rcp);
+    float f[8];
+    Half8<T>::to_float(raw[i], f);
+    int qv[8];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2)
+      quant_two(fmul2(make_float2(f[e], f[e + 1]), mult2), s2, ns2, r2, qv[e], qv[e + 1]);
+    const uint2 codes = make_uint2(pack4_lo_bytes(qv[0], qv[1], qv[2], qv[3]), pack4_lo_bytes(qv[4], qv[5], qv[6], qv[7]));
+    const int sw = (D == 128) ? ((c >> 1) ^ (row & 7)) : ((c >> 1) ^ ((row >> 1) & 3));
+    *reinterpret_cast<uint2*>(qtile + row * D + sw * 16 + (c & 1) * 8) = codes;
+    if (dump && row0 + row < sq.len) *reinterpret_cast<uint2*>(dump + row * D + c * 8) = codes;
+    if (c == 0) {
+      rsc[row] = scale[i];
+      // the codes' scale, once per block: the block's first row
+      if (p.q_scale_out != nullptr && row0 + row < sq.len && ((row0 + row) & ((1 << blk_shift) - 1)) == 0)
+        p.q_scale_out[scale_head + ((row0 + row) >> blk_shift)] = scale[i];
+    }
+  }
+  warpgroup_sync(t);
+  const float own = rsc[row_in_tile];
+  fence_proxy_async_smem();  // the codes are read by tcgen05.mma (async proxy)
+  mbar_arrive(bar_q);
+  return own;
+}
+
 template <class C, int D, bool OBF16>
 __device__ __forceinline__ float fused_q_tile(const AttnParams& p, uint8_t* qtile, float* red, int t, int r,
                                               const SeqSpan& sq, int b, int h, int tile, uint64_t* bar_q) {
@@ -221,9 +328,7 @@ __device__ __forceinline__ float fused_q_tile(const AttnParams& p, uint8_t* qtil
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((r & 31) == 0) red[r >> 5] = amax;
-  // the 128 threads of warpgroup t (named barriers 3 and 4; immediate ids keep the count known)
-  if (t == 0) asm volatile("bar.sync 3, 128;" ::: "memory");
-  else asm volatile("bar.sync 4, 128;" ::: "memory");
+  warpgroup_sync(t);
   amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   const float scale = __fdiv_rn(__fmul_rn(amax, p.q_mult), 127.0f);
   const float rcp = __frcp_rn(scale);
@@ -496,11 +601,18 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH, C16>::NUM_THREADS, 1
     float qs;
     if constexpr (FQ) {
       static_assert(!FLASH && QT == 2, "fused Q quantisation: INT8 path, two query tiles");
-      qs = fused_q_tile<C, D, OBF16>(p, smem + C::OFF_Q + t * C::Q_TILE,
-                                     reinterpret_cast<float*>(smem + C::OFF_QRED) + 4 * t, t, row_in_tile, sq, b, h,
-                                     r0 / C::BM, bar_q);
+      if (p.qblk_shift == 7)
+        qs = fused_q_tile<C, D, OBF16>(p, smem + C::OFF_Q + t * C::Q_TILE,
+                                       reinterpret_cast<float*>(smem + C::OFF_QRED) + 4 * t, t, row_in_tile, sq, b,
+                                       h, r0 / C::BM, bar_q);
+      else
+        qs = fused_q_tile_fine<C, D, OBF16>(p, smem + C::OFF_Q + t * C::Q_TILE,
+                                            reinterpret_cast<float*>(smem + C::OFF_QFINE + t * C::QFINE_BYTES), t,
+                                            row_in_tile, sq, b, h, r0 / C::BM, bar_q, row_in_tile);
     } else {
-      qs = (!FLASH && n > 0) ? p.q_scale[((size_t)b * p.Hq + h) * p.nqb + r0 / C::BM] : 0.0f;
+      // this thread's query row's scale (rows past the sequence end use the last row's block)
+      qs = (!FLASH && n > 0) ? p.q_scale[((size_t)b * p.Hq + h) * p.nqb + (min(row, Sq - 1) >> p.qblk_shift)]
+                             : 0.0f;
     }
     const float* ksp = FLASH ? nullptr : p.k_scale + ((size_t)b * p.Hkv + hkv) * p.nkb;
     float m_run = -INFINITY, l_run = 0.0f;

@@ -160,6 +160,7 @@ struct PrepassParams {
   float q_mult;
   int B, Hq, Hkv, Sq, Skv;  // variable-length batches: Sq / Skv = longest sequence
   int nqb, nkb, nvb, nchunk;
+  int qblk;                 // rows per Q scale block: 128 (quant_block_role), or 1/16/32/64 (qquant_fine_kernel)
   // Variable-length batches (nullable): sequence b owns token rows [cu_q[b], cu_q[b+1]) of Q and
   // [cu_k[b], cu_k[b+1]) of K/V (batch extent 1, q_tokens / k_tokens rows); the int8 / e4m3
   // outputs are [H, tokens, D], the scales and statistics stay per sequence.
@@ -471,6 +472,124 @@ template <typename T, bool PACKED, bool C16>
 __global__ void __launch_bounds__(kKQuantThreads, 8) qquant_kernel(PrepassParams p) {
   __shared__ float red[kKQuantThreads / 32];
   quant_block_role<64, T, 128, 1, PACKED, C16, kKQuantThreads>(p, (int)blockIdx.x, true, red);
+}
+
+// Q quantisation with finer scale blocks than the default 128 rows: p.qblk rows per scale (1 =
+// one scale per token, or 16, 32, 64), as per_block_int8's BLKQ argument allows
+// (triton_impl.py:35, 57, 63). 128 threads per CTA and 128 rows per CTA: thread t loads the
+// 16-byte piece g = t % (D/8) of rows r + i * RPP (r = t / (D/8), i < NP). Block maxima:
+//   * qblk = 1: each row's (D/8) threads are consecutive lanes of one warp, so the row's absmax
+//     is a shuffle reduction over those lanes;
+//   * qblk >= RPP (16, 32, 64 >= 8 or 16 rows per pass): each pass's absmax over the CTA, then
+//     the maximum over the qblk / RPP passes of a block.
+// Scale, quotient and rounding arithmetic as quant_block_role, so the codes are bit-identical to
+// the reference's at that BLKQ. The default 128-row blocks keep quant_block_role.
+template <int D, typename T, bool PACKED, bool C16>
+__global__ void __launch_bounds__(128, (D == 128) ? 3 : 4) qquant_fine_kernel(PrepassParams p) {
+  constexpr int NT = 128, TPR = D / 8, RPP = NT / TPR, NP = 128 / RPP;
+  __shared__ float red[NP][NT / 32];
+  __shared__ float pmax[NP];
+  const int g = threadIdx.x % TPR, r = threadIdx.x / TPR;
+  const int blk = p.qblk;
+  const int nb = p.nqb;                      // scale blocks per (batch, head) = ceil(Sq / qblk)
+  const int ng = (p.Sq + 127) / 128;         // CTAs per head
+  const int cta = blockIdx.x;
+  const int grp = cta % ng;
+  const int hh = (cta / ng) % p.Hq;
+  const int bb = cta / (ng * p.Hq);
+  const SeqSpan sp = seq_span(PACKED ? p.cu_q : nullptr, bb, p.Sq, p.q_tokens);
+  const int S = sp.len;
+  const int row0 = grp * 128;
+  if (row0 >= S) return;  // uniform over the CTA
+  const char* src = reinterpret_cast<const char*>(p.q) +
+                    (sp.batch * p.q_sb + hh * p.q_sh + sp.base * p.q_ss) * (int64_t)sizeof(T) + g * 16;
+  const int64_t ss = p.q_ss * (int64_t)sizeof(T);
+  uint4 raw[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int row = row0 + r + i * RPP;
+    raw[i] = (row < S) ? ldg_nc_v4(src + row * ss) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float m[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) m[i] = Half8<T>::absmax(raw[i]);
+  if (blk == 1) {
+#pragma unroll
+    for (int i = 0; i < NP; ++i)
+#pragma unroll
+      for (int o = TPR / 2; o > 0; o >>= 1) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+  } else {
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+      if ((threadIdx.x & 31) == 0) red[i][threadIdx.x >> 5] = m[i];
+    }
+    __syncthreads();
+    if (threadIdx.x < NP) {
+      float x = red[threadIdx.x][0];
+#pragma unroll
+      for (int w = 1; w < NT / 32; ++w) x = fmaxf(x, red[threadIdx.x][w]);
+      pmax[threadIdx.x] = x;
+    }
+    __syncthreads();
+    const int ppb = blk / RPP;  // passes per scale block
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const int i0 = (i / ppb) * ppb;  // the block's first pass
+      float x = 0.0f;
+      for (int j = 0; j < ppb; ++j) x = fmaxf(x, pmax[i0 + j]);
+      m[i] = x;
+    }
+  }
+  float scale[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) scale[i] = __fdiv_rn(__fmul_rn(m[i], p.q_mult), 127.0f);
+  const size_t head = (size_t)bb * p.Hq + hh;
+  if (blk == 1) {
+    if (g == 0) {
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        const int row = row0 + r + i * RPP;
+        if (row < S) p.q_scale[head * nb + row] = scale[i];
+      }
+    }
+  } else if (r == 0 && g == 0) {
+    // one thread per CTA stores the CTA's block scales: block b spans passes [b*ppb, (b+1)*ppb)
+    const int ppb = blk / RPP;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const int b = (row0 + i * RPP) / blk;
+      if (i % ppb == 0 && b < nb) p.q_scale[head * nb + b] = scale[i];
+    }
+  }
+  const size_t first_row = PACKED ? (size_t)hh * p.q_tokens + sp.base : head * (size_t)S;
+  int8_t* dst = p.q_i8 + first_row * D + g * 8;
+  __half* dst16 = nullptr;
+  if constexpr (C16)
+    dst16 = p.q_c16 + (int64_t)sp.batch * p.qc_sb + (int64_t)hh * p.qc_sh + (int64_t)sp.base * p.qc_ss + g * 8;
+  const float2 mult2 = make_float2(p.q_mult, p.q_mult);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int row = row0 + r + i * RPP;
+    if (row >= S) continue;
+    const float rcp = __frcp_rn(scale[i]);
+    const float2 s2 = make_float2(scale[i], scale[i]), ns2 = make_float2(-scale[i], -scale[i]);
+    const float2 r2 = make_float2(rcp, rcp);
+    float f[8];
+    Half8<T>::to_float(raw[i], f);
+    int qv[8];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) quant_two(fmul2(make_float2(f[e], f[e + 1]), mult2), s2, ns2, r2, qv[e], qv[e + 1]);
+    if constexpr (C16) {
+      *reinterpret_cast<uint4*>(dst16 + (int64_t)row * p.qc_ss) =
+          make_uint4(codes_to_half2(qv[0], qv[1]), codes_to_half2(qv[2], qv[3]), codes_to_half2(qv[4], qv[5]),
+                     codes_to_half2(qv[6], qv[7]));
+    } else {
+      *reinterpret_cast<uint2*>(dst + (size_t)row * D) =
+          make_uint2(pack4_lo_bytes(qv[0], qv[1], qv[2], qv[3]), pack4_lo_bytes(qv[4], qv[5], qv[6], qv[7]));
+    }
+  }
 }
 
 struct FinalizeParams {

@@ -7,7 +7,9 @@ Mirrors kernels/sage_attn/triton_impl.py:
     too (the TriBench ``cuda`` variant entry point).
 Differences from the reference are deliberate and documented: ``causal`` is honoured (the
 Triton kernel ignores it), K is smoothed by default (``smooth_k=True``), P.V can run in FP8
-(``pv="fp8"``), and bf16 inputs keep P and V in bf16 instead of casting V to fp16.
+(``pv="fp8"``), bf16 inputs keep P and V in bf16 instead of casting V to fp16, and the
+attention path accepts Q scale blocks finer than 128 rows (``blkq``: per_block_int8's BLKQ,
+which the reference's own attention kernel does not support, triton_impl.py:136, 148).
 
 torch is used only for device memory, the current stream and dtype/shape bookkeeping; all
 arithmetic runs in libsage_sm100.so. There is no CPU or Triton fallback.
@@ -72,19 +74,23 @@ class SageQuant:
     k_mean: torch.Tensor | None = None
     v_fp8: torch.Tensor | None = None
     v_scale: torch.Tensor | None = None
+    blkq: int = 128  # query rows per q_scale entry
 
 
 def per_block_int8(q, k, km=None, BLKQ=128, BLKK=64, sm_scale=None, tensor_layout="HND", *, smooth_k=False,
                    return_km=False):
-    """INT8 per-block quantisation of Q (128-row blocks) and K (64-row blocks).
+    """INT8 per-block quantisation of Q (BLKQ-row blocks) and K (64-row blocks).
 
     Same contract as the reference per_block_int8 (triton_impl.py:35-82): returns
-    (q_int8 [B,Hq,Sq,D], q_scale [B,Hq,ceil(Sq/128)], k_int8 [B,Hkv,Skv,D], k_scale [B,Hkv,ceil(Skv/64)]);
+    (q_int8 [B,Hq,Sq,D], q_scale [B,Hq,ceil(Sq/BLKQ)], k_int8 [B,Hkv,Skv,D], k_scale [B,Hkv,ceil(Skv/64)]);
+    BLKQ is 128 (default), 64, 32, 16 or 1 (one scale per token), bit-identical to the
+    reference at each; BLKK must be 64 (the attention kernel's K scale granularity).
     ``km`` (broadcastable to [B, Hkv, 1, D]) is subtracted from K in fp32 first. ``smooth_k=True``
     computes km on the device (the K channel mean); ``return_km`` appends it to the tuple.
     """
-    if BLKQ != 128 or BLKK != 64:
-        raise ValueError("the sm_100a kernels use BLKQ=128, BLKK=64 (triton_impl.py:166-167)")
+    if BLKK != 64:
+        raise ValueError("the sm_100a kernels use BLKK=64 (triton_impl.py:167)")
+    qflag = N.qblk_flag(BLKQ)
     _check_tensor("q", q)
     _check_tensor("k", k, q.dtype)
     if q.dtype not in _DTYPES:
@@ -98,7 +104,7 @@ def per_block_int8(q, k, km=None, BLKQ=128, BLKK=64, sm_scale=None, tensor_layou
     dev = q.device
     q_i8 = torch.empty((B, Hq, Sq, D), dtype=torch.int8, device=dev)
     k_i8 = torch.empty((B, Hkv, Skv, D), dtype=torch.int8, device=dev)
-    q_scale = torch.empty((B, Hq, (Sq + 127) // 128), dtype=torch.float32, device=dev)
+    q_scale = torch.empty((B, Hq, (Sq + BLKQ - 1) // BLKQ), dtype=torch.float32, device=dev)
     k_scale = torch.empty((B, Hkv, (Skv + 63) // 64), dtype=torch.float32, device=dev)
     flags = 0
     k_mean = None
@@ -120,7 +126,7 @@ def per_block_int8(q, k, km=None, BLKQ=128, BLKK=64, sm_scale=None, tensor_layou
     with torch.cuda.device(dev):
         rc = lib.sage_per_block_int8(
             _vp(q), _vp(k), _DTYPES[q.dtype], B, Hq, Hkv, Sq, Skv, D, N.strides3(*qs), N.strides3(*ks),
-            ctypes.c_float(0.0 if sm_scale is None else float(sm_scale)), flags,
+            ctypes.c_float(0.0 if sm_scale is None else float(sm_scale)), flags | qflag,
             _vp(q_i8), _vp(q_scale), _vp(k_i8), _vp(k_scale), _vp(k_mean), _vp(ws), ws_n, _stream_ptr(dev))
     N.check("sage_per_block_int8", rc)
     if return_km:
@@ -171,7 +177,7 @@ def attn_fwd(quant: SageQuant, v, causal=False, *, pv="16bit", out_dtype=None, t
         rc = N.load().sage_attn_fwd(
             _vp(q_i8), _vp(quant.q_scale), _vp(k_i8), _vp(quant.k_scale), _vp(vv), N.strides3(*vs),
             _vp(quant.v_scale), _vp(out), N.strides3(*os_), _DTYPES[dt], pv_mode, int(bool(causal)),
-            B, Hq, Hkv, Sq, Skv, D, _stream_ptr(dev))
+            N.qblk_flag(quant.blkq), B, Hq, Hkv, Sq, Skv, D, _stream_ptr(dev))
     N.check("sage_attn_fwd", rc)
     return out
 
@@ -188,16 +194,19 @@ class SagePlan:
       * True: "fused" at either head_dim (no INT8 Q buffer unless ``keep_q_int8``);
       * False: "int8" — INT8 operands from the pre-pass (sage_prepass + sage_attn_fwd).
     "fused" and "int8" give bit-identical output; "codes16" matches them to float rounding.
+    ``blkq``: query rows per Q scale (128, 64, 32, 16 or 1), on every route.
     """
 
     def __init__(self, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, dtype, device, *, pv="16bit",
-                 smooth_k=True, causal=False, sm_scale=None, fused_q=None, keep_q_int8=False):
+                 smooth_k=True, causal=False, sm_scale=None, fused_q=None, keep_q_int8=False, blkq=128):
         if dtype not in _DTYPES:
             raise TypeError(f"dtype must be float16 or bfloat16, got {dtype}")
         self.shape = (batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)
         self.dtype, self.device = dtype, torch.device(device)
         self.pv_mode = _PV[pv]
-        self.flags = N.SAGE_FLAG_SMOOTH_K if smooth_k else 0
+        self.blkq = int(blkq)
+        self.qflag = N.qblk_flag(self.blkq)
+        self.flags = (N.SAGE_FLAG_SMOOTH_K if smooth_k else 0) | self.qflag
         if fused_q is None:
             self.route = "fused" if head_dim == 128 else "codes16"
         else:
@@ -211,13 +220,14 @@ class SagePlan:
         want_k = self.route != "codes16"
         self.quant = SageQuant(
             q_int8=torch.empty((B, Hq, Sq, D), dtype=torch.int8, device=dev) if want_q else None,
-            q_scale=torch.empty((B, Hq, (Sq + 127) // 128), dtype=torch.float32, device=dev)
+            q_scale=torch.empty((B, Hq, (Sq + self.blkq - 1) // self.blkq), dtype=torch.float32, device=dev)
             if (want_q or self.route == "codes16") else None,
             k_int8=torch.empty((B, Hkv, Skv, D), dtype=torch.int8, device=dev) if want_k else None,
             k_scale=torch.empty((B, Hkv, (Skv + 63) // 64), dtype=torch.float32, device=dev),
             k_mean=torch.empty((B, Hkv, D), dtype=torch.float32, device=dev) if smooth_k else None,
             v_fp8=torch.empty((B, Hkv, Skv, D), dtype=torch.uint8, device=dev) if self.pv_mode else None,
             v_scale=torch.empty((B, Hkv, D), dtype=torch.float32, device=dev) if self.pv_mode else None,
+            blkq=self.blkq,
         )
         self.codes16 = None  # (q, k) fp16 code buffers of the split form, allocated by prepass()
         self.ws_bytes = int(N.load().sage_workspace_bytes(B, Hkv, Skv, D, self.pv_mode, self.flags | self.route_flag))
@@ -275,7 +285,7 @@ class SagePlan:
             rc = lib.sage_attn_fwd_codes16(
                 _vp(self.codes16[0]), _vp(qd.q_scale), _vp(self.codes16[1]), _vp(qd.k_scale), _vp(vv),
                 N.strides3(*vs), _vp(qd.v_scale), _vp(out), N.strides3(*os_), _DTYPES[self.dtype], self.pv_mode,
-                int(self.causal), B, Hq, Hkv, Sq, Skv, D, _stream_ptr(self.device))
+                int(self.causal), self.qflag, B, Hq, Hkv, Sq, Skv, D, _stream_ptr(self.device))
             N.check("sage_attn_fwd_codes16", rc)
             return out
         if q is None:
@@ -283,8 +293,8 @@ class SagePlan:
         *_, qs = _dims(q, tensor_layout)
         rc = lib.sage_attn_fwd_fused_q(
             _vp(q), N.strides3(*qs), self._sm_scale(), _vp(qd.k_int8), _vp(qd.k_scale), _vp(vv), N.strides3(*vs),
-            _vp(qd.v_scale), _vp(out), N.strides3(*os_), _DTYPES[self.dtype], self.pv_mode, int(self.causal), B, Hq,
-            Hkv, Sq, Skv, D, _vp(qd.q_int8), _vp(qd.q_scale), _stream_ptr(self.device))
+            _vp(qd.v_scale), _vp(out), N.strides3(*os_), _DTYPES[self.dtype], self.pv_mode, int(self.causal),
+            self.qflag, B, Hq, Hkv, Sq, Skv, D, _vp(qd.q_int8), _vp(qd.q_scale), _stream_ptr(self.device))
         N.check("sage_attn_fwd_fused_q", rc)
         return out
 
@@ -356,7 +366,7 @@ class HostPipeline:
     """
 
     def __init__(self, batch, heads_q, heads_kv, seq_q, seq_kv, head_dim, dtype, device, *, chunks=16,
-                 pv="16bit", smooth_k=True, causal=False, sm_scale=None):
+                 pv="16bit", smooth_k=True, causal=False, sm_scale=None, blkq=128):
         if heads_kv <= 0 or heads_q % heads_kv:
             raise ValueError(f"heads_q ({heads_q}) must be a multiple of heads_kv ({heads_kv})")
         self.shape = (batch, heads_q, heads_kv, seq_q, seq_kv, head_dim)
@@ -372,7 +382,7 @@ class HostPipeline:
             m = b - a
             if m not in self.plans:
                 self.plans[m] = SagePlan(1, m * self.groups, m, seq_q, seq_kv, head_dim, dtype, self.device, pv=pv,
-                                         smooth_k=smooth_k, causal=causal, sm_scale=sm_scale)
+                                         smooth_k=smooth_k, causal=causal, sm_scale=sm_scale, blkq=blkq)
         mmax = max(b - a for a, b in self.ranges)
         g = self.groups
         self.slots = [dict(q=torch.empty((1, mmax * g, seq_q, head_dim), dtype=dtype, device=self.device),
@@ -427,12 +437,14 @@ class HostPipeline:
 
 
 def run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=True, tensor_layout="HND",
-                  out=None, fused_q=None):
+                  out=None, fused_q=None, blkq=128):
     """Drop-in for run_sage_attn (triton_impl.py:162-200) on sm_100a.
 
     q: [B, Hq, Sq, D], k/v: [B, Hkv, Skv, D] (HND; NHD with tensor_layout="NHD"), fp16 or bf16,
     D in {64, 128}. Returns o with q's shape and dtype. ``fused_q``: where Q is quantised
-    (SagePlan; None = sage_run's choice); the output is bit-identical either way.
+    (SagePlan; None = sage_run's choice); the output is bit-identical either way. ``blkq``:
+    query rows per Q scale (128 is the reference's scheme; 64, 32, 16 or 1 = per token are
+    finer, for inputs whose query rows have outliers).
     """
     _check_tensor("q", q)
     for name, t in (("k", k), ("v", v)):
@@ -444,7 +456,7 @@ def run_sage_attn(q, k, v, causal=False, sm_scale=None, *, pv="16bit", smooth_k=
     B, Hq, Sq, D, _ = _dims(q, tensor_layout)
     _, Hkv, Skv, _, _ = _dims(k, tensor_layout)
     plan = SagePlan(B, Hq, Hkv, Sq, Skv, D, q.dtype, q.device, pv=pv, smooth_k=smooth_k, causal=causal,
-                    sm_scale=sm_scale, fused_q=fused_q)
+                    sm_scale=sm_scale, fused_q=fused_q, blkq=blkq)
     with torch.cuda.device(q.device):
         return plan.run(q, k, v, out=out, tensor_layout=tensor_layout)
 

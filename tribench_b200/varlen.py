@@ -112,19 +112,20 @@ class _Batch:
 
 
 def per_block_int8_varlen(q, k, cu_seqlens_q, cu_seqlens_k, max_seqlen_q=None, max_seqlen_k=None, sm_scale=None,
-                          *, smooth_k=False, km=None, return_km=False):
+                          *, smooth_k=False, km=None, return_km=False, BLKQ=128):
     """per_block_int8 for packed sequences. Returns (q_int8 [Hq, total_q, D],
-    q_scale [B, Hq, ceil(max_seqlen_q/128)], k_int8 [Hkv, total_k, D],
+    q_scale [B, Hq, ceil(max_seqlen_q/BLKQ)], k_int8 [Hkv, total_k, D],
     k_scale [B, Hkv, ceil(max_seqlen_k/64)]) (+ k_mean [B, Hkv, D] with ``return_km``).
     Scale entries past a sequence's own block count are left unwritten. ``km`` ([B, Hkv, D]
     fp32) is the caller's per-sequence channel mean; ``smooth_k`` computes it on the device."""
+    qflag = N.qblk_flag(BLKQ)
     bt = _Batch(q, k, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, False)
     if bt.empty:
         raise ValueError("per_block_int8_varlen needs at least one query and one key token")
     dev, D = bt.dev, bt.D
     q_i8 = torch.empty((bt.Hq, bt.Tq, D), dtype=torch.int8, device=dev)
     k_i8 = torch.empty((bt.Hkv, bt.Tk, D), dtype=torch.int8, device=dev)
-    q_scale = torch.empty((bt.B, bt.Hq, (bt.max_q + 127) // 128), dtype=torch.float32, device=dev)
+    q_scale = torch.empty((bt.B, bt.Hq, (bt.max_q + BLKQ - 1) // BLKQ), dtype=torch.float32, device=dev)
     k_scale = torch.empty((bt.B, bt.Hkv, (bt.max_k + 63) // 64), dtype=torch.float32, device=dev)
     flags, k_mean = 0, None
     if km is not None:
@@ -139,7 +140,7 @@ def per_block_int8_varlen(q, k, cu_seqlens_q, cu_seqlens_k, max_seqlen_q=None, m
         rc = N.load().sage_per_block_int8_varlen(
             _vp(q), _vp(k), _DTYPES[q.dtype], bt.B, bt.Hq, bt.Hkv, bt.Tq, bt.Tk, bt.max_q, bt.max_k, D,
             _vp(bt.cu_q), _vp(bt.cu_k), N.strides2(*bt.qs), N.strides2(*bt.ks),
-            ctypes.c_float(0.0 if sm_scale is None else float(sm_scale)), flags,
+            ctypes.c_float(0.0 if sm_scale is None else float(sm_scale)), flags | qflag,
             _vp(q_i8), _vp(q_scale), _vp(k_i8), _vp(k_scale), _vp(k_mean), _vp(ws), ws_n, _stream_ptr(dev))
     N.check("sage_per_block_int8_varlen", rc)
     if return_km:
@@ -162,11 +163,13 @@ def _out_and_v(bt: _Batch, q, v, out):
 
 
 def run_sage_attn_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q=None, max_seqlen_k=None, causal=False,
-                         sm_scale=None, *, pv="16bit", smooth_k=True, out=None, fused_q=None):
+                         sm_scale=None, *, pv="16bit", smooth_k=True, out=None, fused_q=None, blkq=128):
     """run_sage_attn for packed sequences: q [total_q, Hq, D], k/v [total_k, Hkv, D] -> o like q.
     A sequence with query rows but no keys gets o = 0. ``fused_q`` picks the operand route as
     SagePlan does (None: Q quantised in the attention kernel at head_dim 128, fp16 codes at 64;
-    True: Q in the kernel; False: INT8 operands from the pre-pass)."""
+    True: Q in the kernel; False: INT8 operands from the pre-pass). ``blkq``: query rows per Q
+    scale (128, 64, 32, 16 or 1), counted from each sequence's first token."""
+    qflag = N.qblk_flag(blkq)
     bt = _Batch(q, k, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal)
     vs, out, os_ = _out_and_v(bt, q, v, out)
     if bt.Tq == 0:
@@ -180,13 +183,13 @@ def run_sage_attn_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q=None,
     route_flag = {"fused": N.SAGE_FLAG_FUSED_Q, "int8": N.SAGE_FLAG_PREPASS_Q, "codes16": 0}[route]
     q_i8 = torch.empty((bt.Hq, bt.Tq, D), dtype=torch.int8, device=dev) if route == "int8" else None
     k_i8 = torch.empty((bt.Hkv, bt.Tk, D), dtype=torch.int8, device=dev) if route != "codes16" else None
-    q_scale = None if route == "fused" else torch.empty((bt.B, bt.Hq, (bt.max_q + 127) // 128), dtype=torch.float32,
-                                                        device=dev)
+    q_scale = None if route == "fused" else torch.empty((bt.B, bt.Hq, (bt.max_q + blkq - 1) // blkq),
+                                                        dtype=torch.float32, device=dev)
     k_scale = torch.empty((bt.B, bt.Hkv, (bt.max_k + 63) // 64), dtype=torch.float32, device=dev)
     k_mean = torch.empty((bt.B, bt.Hkv, D), dtype=torch.float32, device=dev) if smooth_k else None
     v_fp8 = torch.empty((bt.Hkv, bt.Tk, D), dtype=torch.uint8, device=dev) if fp8 else None
     v_scale = torch.empty((bt.B, bt.Hkv, D), dtype=torch.float32, device=dev) if fp8 else None
-    flags = (N.SAGE_FLAG_SMOOTH_K if smooth_k else 0) | route_flag
+    flags = (N.SAGE_FLAG_SMOOTH_K if smooth_k else 0) | route_flag | qflag
     ws_n = int(N.load().sage_workspace_bytes(bt.B, bt.Hkv, bt.max_k, D, pv_mode, flags))
     ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
