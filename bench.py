@@ -8,15 +8,22 @@ quantisation, + FP8 V for c4) followed by the fused attention kernel, on inputs 
 resident in HBM. The default workload is "h8k" — B=2, H=32, S=8192, D=128, fp16, non-causal,
 smoothed K, fp16 P.V — the S=8K D=128 configuration the headline metric is quoted on.
 
-Multi-GPU (torchrun, one process per GPU): weak scaling over the (batch x head) grid. The
-global job at N ranks is the workload with batch N times larger; rank r generates and
-processes its own batches (no collective on the data path). value = total ops of all ranks /
-max-over-ranks device time.
+Multi-GPU (torchrun, one process per GPU): the (batch x head) grid is partitioned across the
+ranks and a step ends when the whole output is assembled on rank 0 — the north star's only
+collective, the final output gather: every rank computes its heads in --waves waves and sends
+each finished wave to rank 0 (NCCL point to point) while it computes the next one. The default
+workloads scale weakly (the global batch at N ranks is N times the 1-GPU batch, so N=1 is the
+1-GPU line exactly, with no gather); the sharded long-context workload "c5" (B=16, H=64, S=32K,
+causal) scales strongly (its fixed 1024-head grid is split). value = total ops of all ranks /
+max-over-ranks device time, gather included.
 
-The sharded long-context workload "c5" (B=16, H=64, S=32K, causal) scales strongly instead:
-the fixed 1024-head grid is split across the ranks, each rank computes its heads in --waves
-waves, and a step ends when the whole output is assembled on rank 0: every other rank sends
-each finished wave to rank 0 (NCCL point to point) while it computes the next one.
+Rooflines divide by the tcgen05 rates measured on this hardware (profiles/tensor_peaks.json,
+made by `python -m tribench_b200.peaks`): ops per SM clock x SMs x the SM clock the timed
+region ran at (the max clock when the run held it).
+
+At N=1 the line also carries the reference's own Triton kernel (run_sage_attn /
+run_flash_attn from the installed TriBench in baseline/_ref) timed with CUDA events on the
+same device-resident inputs, and the default step with one Q scale per token (blkq=1).
 
 --workload fa_s4k_d64 | fa_s8k_d64 benchmarks the flash_attn pack (fp16 QK^T and P.V, no
 quantisation; its meta.json cases) through sage_flash_attn_fwd, one launch per step.
@@ -61,7 +68,11 @@ def parse():
     ap.add_argument("--e2e-chunks", type=int, default=16, help="head chunks of the host pipeline (e2e)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--waves", type=int, default=8, help="head waves per rank (sharded c5 workload)")
+    ap.add_argument("--waves", type=int, default=None,
+                    help="head waves per rank when gathering (default: 8 for c5, 4 otherwise)")
+    ap.add_argument("--no-triton-reference", action="store_true",
+                    help="skip timing the reference's Triton kernel (baseline/_ref) at N=1")
+    ap.add_argument("--no-blkq1", action="store_true", help="skip the per-token (blkq=1) side measurement")
     ap.add_argument("--no-tribench-timing", action="store_true",
                     help="skip the drop-in run() measured with TriBench's do_bench procedure")
     return ap.parse_args()
@@ -99,6 +110,94 @@ def read_peaks() -> dict:
     return {"bf16_burst": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
 
 
+def read_tensor_peaks() -> dict | None:
+    """Per-SM-clock tcgen05 rates and the sustained (power-capped) rates measured by
+    tribench_b200.peaks (profiles/tensor_peaks.json), or None."""
+    path = os.path.join(ROOT, "profiles", "tensor_peaks.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f)
+
+
+def tensor_rooflines(tp: dict | None, clock_mhz, ops_qk: float, ops_pv: float, pv: str) -> dict:
+    """Peaks (TOPS) for the attention kernel: INT8 QK^T and 16-bit or e4m3 P.V at their measured
+    per-clock rates, at the clock the timed region ran at (the max clock when the median sample
+    is within 5 % of it); the mixed peak is the harmonic combination for these op counts. Also
+    the sustained (power-capped, seconds-long) mixed rate from the same measurement."""
+    pv_kind = "e4m3" if pv == "fp8" else "f16"
+    if tp is None:  # fallback: the driver's cuBLAS bf16 figure, INT8 / FP8 at twice it
+        pk = read_peaks()
+        i8, pvr = 2 * pk["bf16_burst"], (2 if pv == "fp8" else 1) * pk["bf16_burst"]
+        return {"int8": i8, "pv": pvr, "mixed": (ops_qk + ops_pv) / (ops_qk / i8 + ops_pv / pvr), "clock_mhz": None,
+                "source": f"{pk['source']} cuBLAS bf16 burst x2 (no tcgen05 measurement)"}
+    max_mhz = tp["max_sm_mhz"]
+    use = max_mhz if (clock_mhz is None or clock_mhz >= 0.95 * max_mhz) else float(clock_mhz)
+    rate = lambda k: tp["ops_per_clk_per_sm"][k]["128"] * tp["sms"] * use * 1e6 / 1e12
+    i8, pvr = rate("i8"), rate(pv_kind)
+    si8, spv = tp["sustained"]["i8"]["tops"], tp["sustained"][pv_kind]["tops"]
+    return {"int8": round(i8, 1), "pv": round(pvr, 1), "mixed": round((ops_qk + ops_pv) / (ops_qk / i8 + ops_pv / pvr), 1),
+            "mixed_sustained": round((ops_qk + ops_pv) / (ops_qk / si8 + ops_pv / spv), 1),
+            "int8_sustained": si8, "clock_mhz": use,
+            "source": f"measured tcgen05 rates (profiles/tensor_peaks.json): {tp['ops_per_clk_per_sm']['i8']['128']:.0f} "
+                      f"int8 / {tp['ops_per_clk_per_sm'][pv_kind]['128']:.0f} {pv_kind} ops per SM clock x {tp['sms']} "
+                      f"SMs x {use:.0f} MHz" + (" (max clock; the run held it)" if use == max_mhz else
+                                               " (the run's median SM clock)")}
+
+
+def load_triton_reference(pack: str):
+    """The reference's own Triton entry point from the TriBench installed in baseline/_ref
+    (run_sage_attn, kernels/sage_attn/triton_impl.py:162; run_flash_attn,
+    kernels/flash_attn/triton_impl.py:110), or (None, reason)."""
+    import importlib.util
+
+    path = os.path.join(ROOT, "baseline", "_ref", "kernels", pack, "triton_impl.py")
+    if not os.path.exists(path):
+        return None, f"no installed reference at {os.path.relpath(path, ROOT)}"
+    try:
+        spec = importlib.util.spec_from_file_location(f"tribench_ref_{pack}_triton_impl", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return getattr(mod, "run_sage_attn" if pack == "sage_attn" else "run_flash_attn"), None
+    except Exception as e:  # pragma: no cover - reported in the line
+        return None, f"{type(e).__name__}: {str(e).splitlines()[0] if str(e) else ''}"
+
+
+def time_triton_reference(pack: str, q, k, v, causal: bool, ops: float, our_ms: float, ours=None, reps: int = 20):
+    """CUDA-event time of the reference's Triton kernel on the same device-resident inputs."""
+    fn, why = load_triton_reference(pack)
+    if fn is None:
+        return {"unavailable": why}
+    out = {"call": f"{pack} triton_impl.{'run_sage_attn' if pack == 'sage_attn' else 'run_flash_attn'}"
+                   "(q, k, v) from baseline/_ref (stock reference code, Triton-compiled for this GPU)",
+           "note": "the reference's Triton kernels ignore causal; timed non-causal only"}
+    if causal:
+        out["unavailable"] = "causal workload: the reference's Triton sage kernel ignores causal"
+        return out
+    try:
+        for _ in range(3):
+            o = fn(q, k, v)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        times = []
+        for _ in range(reps):
+            e0.record()
+            fn(q, k, v)
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+    except Exception as e:
+        out["unavailable"] = f"{type(e).__name__}: {str(e).splitlines()[0] if str(e) else ''}"
+        return out
+    p50 = statistics.median(times)
+    out.update({"p50_ms": round(p50, 4), "min_ms": round(min(times), 4), "reps": reps,
+                "value": round(ops / (p50 * 1e-3) / 1e12, 2),
+                "speedup_ours_vs_triton": round(p50 / our_ms, 3)})
+    if ours is not None:
+        out["max_abs_diff_vs_ours"] = float((o.float() - ours.float()).abs().max().item())
+    return out
+
+
 def read_traffic() -> dict:
     path = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(path):
@@ -108,12 +207,13 @@ def read_traffic() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every INTERVAL_MS while the warm-up and timed
-    steps run; the summary's sm_mhz is the median over those samples (under load)."""
+    """nvidia-smi clocks/throttle reasons sampled every INTERVAL_MS; summary() describes the
+    samples taken after mark() (call it when the warm-up steps start), so the median SM clock
+    is that of the loaded GPU during warm-up + timed steps."""
 
     INTERVAL_MS = 20
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -121,6 +221,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.file = None
+        self.t_mark = None
 
     def __enter__(self):
         try:
@@ -132,6 +233,11 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def mark(self):
+        import datetime
+
+        self.t_mark = datetime.datetime.now()
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -141,30 +247,38 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        import datetime
+
         if self.proc is None or self.file is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()
         with open(self.file.name) as f:
             rows = [r.strip().split(", ") for r in f if r.strip()]
         os.unlink(self.file.name)
-        sm, smax, power, reasons = [], None, [], set()
+        sm, smax, power, reasons, n_all = [], None, [], set(), 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
-            if len(r) < 9:
+            if len(r) < 10:
                 continue
             try:
-                sm.append(float(r[1]))
-                smax = float(r[2])
-                power.append(float(r[3]))
+                ts = datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f")
+                clk, cmax, pw = float(r[2]), float(r[3]), float(r[4])
             except ValueError:
                 continue
-            for n, v in zip(names, r[5:9]):
+            n_all += 1
+            if self.t_mark is not None and ts < self.t_mark:
+                continue
+            sm.append(clk)
+            smax = cmax
+            power.append(pw)
+            for n, v in zip(names, r[6:10]):
                 if v.strip().lower() == "active":
                     reasons.add(n)
-        loaded = [s for s, p in zip(sm, power) if p > 300.0] or sm
-        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm), "samples_under_load": len(loaded),
-                "interval_ms": self.INTERVAL_MS, "over": "warm-up + timed steps (median of samples above 300 W)",
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "sm_mhz_min": min(sm) if sm else None, "reasons": sorted(reasons), "samples": len(sm),
+                "samples_all": n_all, "interval_ms": self.INTERVAL_MS,
+                "over": "warm-up + timed steps (samples after the first warm-up step was queued)",
+                "power_w_median": statistics.median(power) if power else None,
                 "power_w_max": max(power) if power else None}
 
 
@@ -306,6 +420,7 @@ def main_flash(args):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
         time.sleep(0.3)
+        clk.mark()
         for _ in range(args.warmup):
             tb.run_flash_attn(q, k, v, causal=case["causal"], out=o)
         torch.cuda.synchronize(dev)
@@ -353,11 +468,19 @@ def main_flash(args):
         tri = timing.summarize(lat, flops=est_total["flops"])
         tri["call"] = "tribench_b200.run_flash_attn(q, k, v, causal) (the plugin's run; output allocated per call)"
         tri["timer"] = "do_bench restated without Triton: 256 MB L2 flush per rep, warmup 200 ms, rep 2000 ms"
+    triton_ref = None
+    if world == 1 and not args.no_triton_reference:
+        B_, H_, S_, D_ = case["batch_size"], case["num_heads"], case["seq_len"], case["head_dim"]
+        qv, kv_, vv = (t.view(B_, H_, S_, D_) for t in (q, k, v))
+        triton_ref = time_triton_reference("flash_attn", qv, kv_, vv, case["causal"], est_total["ops_alg"],
+                                           statistics.median(launch_ms), ours=o.view(B_, H_, S_, D_))
     cpu = cpu_baseline(dict(case, seq_len=case["seq_len"]), args.cpu_baseline_seconds) \
         if rank == 0 and world == 1 and not args.no_cpu_baseline else None
     if rank == 0:
-        peaks = read_peaks()
-        bf16 = peaks["bf16_sustained"]
+        clocks = clk.summary()
+        # both products at the fp16 rate: the mixed roofline with P.V's kind for QK^T too
+        rl = tensor_rooflines(read_tensor_peaks(), clocks.get("sm_mhz"), 0.0, 1.0, "16bit")
+        bf16 = rl["pv"]
         value = est_total["ops_alg"] * args.steps / (total_ms * 1e-3) / 1e12
         achieved = est_rank["ops_alg"] / (statistics.mean(launch_ms) * 1e-3) / 1e12
         line = {
@@ -370,8 +493,11 @@ def main_flash(args):
             "config": config_dict(case, world),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
                          "frac": round(achieved / bf16, 4), "traffic": None, "kernel": "sage_attn_kernel (FLASH)",
-                         "peak_source": f"{peaks['source']} bf16 sustained (dense fp16/bf16 rate)"},
-            "clocks": clk.summary(),
+                         "peak_source": rl["source"] + " (the fp16 rate for both products)",
+                         "peak_sustained": rl.get("mixed_sustained"),
+                         "frac_vs_sustained": round(achieved / rl["mixed_sustained"], 4)
+                         if rl.get("mixed_sustained") else None},
+            "clocks": clocks,
             "e2e": {"value": round(est_total["ops_alg"] * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
                     "d2h_bytes_per_step": o.numel() * o.element_size(),
@@ -380,6 +506,8 @@ def main_flash(args):
         }
         if tri is not None:
             line["tribench_timing"] = {k_: (round(v_, 5) if isinstance(v_, float) else v_) for k_, v_ in tri.items()}
+        if triton_ref is not None:
+            line["triton_reference"] = triton_ref
         if cpu is not None:
             cpu["unit"] = "TFLOP/s"
             line["cpu_baseline"] = cpu
@@ -414,20 +542,30 @@ def main():
     case = workload_case(args.workload, world)
     B, H, S, D = case["batch_size"], case["num_heads"], case["seq_len"], case["head_dim"]
     strong = case["shard"] == "strong"
+    gather = world > 1  # the final output gather to rank 0
     sd = shard.make_shard(case, rank, world)
     nh_total, lo, hi = sd.total, sd.lo, sd.hi
     inp = tb.make_inputs(case, dev, seed=case["seed"], dtype=case["dtype"], heads=(lo, hi))
     q, k, v = inp["q"], inp["k"], inp["v"]
     causal, pv = case["causal"], case["pv"]
-    n_waves = max(1, args.waves) if strong else 1
+    if strong:
+        n_waves = args.waves or 8
+    else:
+        n_waves = (args.waves or 4) if gather else 1
     waves = shard.wave_ranges(lo, hi, n_waves)
-    plans = {}
-    for (a, b) in waves:
-        if b - a not in plans:
-            plans[b - a] = tb.SagePlan(1, b - a, b - a, S, S, D, q.dtype, dev, pv=pv, smooth_k=True, causal=causal)
+
+    def make_plans(blkq=128):
+        out = {}
+        for (a, b) in waves:
+            if b - a not in out:
+                out[b - a] = tb.SagePlan(1, b - a, b - a, S, S, D, q.dtype, dev, pv=pv, smooth_k=True, causal=causal,
+                                         blkq=blkq)
+        return out
+
+    plans = make_plans()
     plan = plans[waves[0][1] - waves[0][0]]
     full = None
-    if strong and rank == 0:
+    if gather and rank == 0:
         # the whole job's output lives on rank 0; its own heads are computed straight into it
         full = torch.empty((1, nh_total, S, D), dtype=q.dtype, device=dev)
         o = full[:, lo:hi]
@@ -447,9 +585,9 @@ def main():
     # one wave = pre-pass + attention over a range of heads: the two C calls sage_run makes
     # (sage_prepass, then sage_attn_fwd, or at head_dim 128 sage_attn_fwd_fused_q, which quantises
     # Q itself), split so that CUDA events bracket the attention kernel
-    def wave(a, b, ev=None):
+    def wave(a, b, ev=None, pls=None):
         i, j = a - lo, b - lo
-        pl = plans[j - i]
+        pl = (pls or plans)[j - i]
         if ev is not None:
             ev[0].record(stream)
         pl.prepass(q[:, i:j], k[:, i:j], v[:, i:j])
@@ -459,16 +597,17 @@ def main():
         if ev is not None:
             ev[2].record(stream)
 
-    # one step = every wave of this rank, then (sharded workload, N > 1) the output gather
-    def step(wave_events=None):
+    # one step = every wave of this rank, then (N > 1) the output gather to rank 0, each wave
+    # sent while the next one is computed
+    def step(wave_events=None, pls=None):
         if flush is not None:
             flush.zero_()
         it = iter(wave_events) if wave_events is not None else None
 
         def compute(a, b):
-            wave(a, b, next(it) if it is not None else None)
+            wave(a, b, next(it) if it is not None else None, pls)
 
-        if strong and world > 1:
+        if gather:
             shard.gather_to(0, o, sd, full, waves=n_waves, compute=compute, timeout_s=300.0)
         else:
             for (a, b) in waves:
@@ -481,6 +620,7 @@ def main():
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
         time.sleep(0.3)  # let nvidia-smi start before the GPU is loaded
+        clk.mark()
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize(dev)
@@ -502,10 +642,13 @@ def main():
     attn_ms = [sum(w[1].elapsed_time(w[2]) for w in evs[i]) for i in range(args.steps)]
     pre_ms = [sum(w[0].elapsed_time(w[1]) for w in evs[i]) for i in range(args.steps)]
     status = tb.device_status(dev)
+    compute_ms = statistics.mean(a + b for a, b in zip(attn_ms, pre_ms))
     if pg is not None:
-        t = torch.tensor([total_ms], device=dev)
+        t = torch.tensor([total_ms, compute_ms], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        total_ms = float(t.item())
+        total_ms, compute_ms_max = float(t[0].item()), float(t[1].item())
+    else:
+        compute_ms_max = compute_ms
 
     # ---- end to end through the public API: host (pinned) inputs -> device -> run -> host output
     e2e_ms = None
@@ -521,6 +664,41 @@ def main():
         tri["call"] = "tribench_b200.run(q, k, v, causal) (the plugin's run; output allocated per call)"
         tri["timer"] = "do_bench restated without Triton: 256 MB L2 flush per rep, warmup 200 ms, rep 2000 ms"
 
+    # the same step with one Q scale per token (blkq=1), beside the default 128-row blocks
+    blkq1 = None
+    if world == 1 and not args.no_blkq1:
+        p1 = make_plans(blkq=1)
+        reps = max(3, min(args.steps, 50))
+        for _ in range(3):
+            step(pls=p1)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            step(pls=p1)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms1 = e0.elapsed_time(e1) / reps
+        # the default step again right after, so both see the same clock
+        e0.record(stream)
+        for _ in range(reps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms128 = e0.elapsed_time(e1) / reps
+        blkq1 = {"ms_per_step": round(ms1, 4), "value": round(est_total["ops_alg"] / (ms1 * 1e-3) / 1e12, 2),
+                 "default_ms_per_step_same_window": round(ms128, 4), "steps": reps,
+                 "note": "one Q scale per token (per_block_int8 BLKQ=1) on every route; same step otherwise"}
+        del p1
+        assert tb.device_status(dev) == 0
+
+    # the reference's own Triton kernel on the same inputs (non-causal only: it ignores causal)
+    triton_ref = None
+    if world == 1 and not args.no_triton_reference:
+        qv, kv_, vv = (t.view(B, H, S, D) for t in (q, k, v))
+        triton_ref = time_triton_reference("sage_attn", qv, kv_, vv, causal, est_total["ops_alg"],
+                                           statistics.median(step_ms), ours=o.view(B, H, S, D))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(case, args.cpu_baseline_seconds)
@@ -528,17 +706,12 @@ def main():
     if rank == 0:
         ops_total = est_total["ops_alg"]
         value = ops_total * args.steps / (total_ms * 1e-3) / 1e12
-        peaks = read_peaks()
-        # Attention kernel roofline: QK^T at the INT8 rate (2x the measured dense bf16 rate) and
-        # P.V at the 16-bit rate (fp16 P.V) or the FP8 rate (FP8 P.V); the binding peak for the
-        # mix of equal op counts is the harmonic combination.
-        bf16 = peaks["bf16_sustained"]
-        pv_rate = bf16 if pv != "fp8" else 2 * bf16
-        mixed_peak = (est_rank["ops_qk"] + est_rank["ops_pv"]) / (est_rank["ops_qk"] / (2 * bf16) +
-                                                                  est_rank["ops_pv"] / pv_rate)
+        clocks = clk.summary()
+        rl = tensor_rooflines(read_tensor_peaks(), clocks.get("sm_mhz"), est_rank["ops_qk"], est_rank["ops_pv"], pv)
         attn_avg = statistics.mean(attn_ms)
         achieved = est_rank["ops_alg"] / (attn_avg * 1e-3) / 1e12
         traffic = read_traffic().get(f"attn_{args.workload}_bytes_per_launch")
+        peaks = read_peaks()
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
@@ -547,18 +720,25 @@ def main():
             "dtype": "int8 QK^T + " + ("e4m3" if pv == "fp8" else case["dtype"]) + " P.V (fp32 accumulate)",
             "data": "synthetic (seeded per (batch, head) slab; BASELINE distributions)",
             "config": config_dict(case, world),
-            "frac_of_int8_peak": round(value / world / (2 * bf16), 4),
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(mixed_peak, 1),
-                         "unit": "TFLOP/s", "frac": round(achieved / mixed_peak, 4), "traffic": traffic,
-                         "kernel": "sage_attn_kernel", "peak_source": f"{peaks['source']} bf16 sustained "
-                         f"{bf16} TF/s: QK^T at 2x (INT8), P.V at {'2x (FP8)' if pv == 'fp8' else '1x (fp16)'}",
+            "frac_of_int8_peak": round(value / world / rl["int8"], 4),
+            "int8_peak": {"tops": rl["int8"], "sustained_tops": rl.get("int8_sustained"),
+                          "frac_vs_sustained": round(value / world / rl["int8_sustained"], 4)
+                          if rl.get("int8_sustained") else None, "source": rl["source"]},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": rl["mixed"],
+                         "unit": "TFLOP/s", "frac": round(achieved / rl["mixed"], 4), "traffic": traffic,
+                         "kernel": "sage_attn_kernel",
+                         "peak_source": rl["source"] + f": QK^T at the int8 rate ({rl['int8']} TOPS), P.V at the "
+                                        f"{'e4m3' if pv == 'fp8' else 'fp16'} rate ({rl['pv']} TOPS), harmonic mix",
+                         "peak_sustained_mixed": rl.get("mixed_sustained"),
+                         "frac_vs_sustained_mixed": round(achieved / rl["mixed_sustained"], 4)
+                         if rl.get("mixed_sustained") else None,
                          "attn_ms": round(attn_avg, 4), "prepass_ms": round(statistics.mean(pre_ms), 4)},
             "prepass_roofline": {"bound": "hbm", "achieved": round(tb.prepass_bytes(dict(case, batch_size=1,
                                  num_heads=hi - lo), fused_q=plan.fused_q) / (statistics.mean(pre_ms) * 1e-3) / 1e9, 1),
                                  "peak": peaks["hbm"], "unit": "GB/s",
                                  "kernels": "kv_stats + kv_finalize + quant (3 launches)",
                                  "q_quantised_in": "attention kernel" if plan.fused_q else "pre-pass"},
-            "clocks": clk.summary(),
+            "clocks": clocks,
             "e2e": None if e2e_ms is None else {
                 "value": round(ops_total * args.e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT,
                 "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
@@ -569,12 +749,20 @@ def main():
             "waves_per_rank": len(waves),
             "device_status": status,
         }
+        if gather:
+            line["gather"] = {"dst_rank": 0,
+                              "bytes_received_per_step": (nh_total - (hi - lo)) * S * D * q.element_size(),
+                              "overlapped": "each rank sends wave w while computing wave w+1",
+                              "compute_ms_per_step_max_over_ranks": round(compute_ms_max, 4),
+                              "exposed_ms_per_step": round(total_ms / args.steps - compute_ms_max, 4)}
         if strong:
-            line["gather"] = {"dst_rank": 0, "bytes_received_per_step": (nh_total - (hi - lo)) * S * D * q.element_size(),
-                              "overlapped": "each rank sends wave w while computing wave w+1"}
             line["e2e_note"] = "not measured for the sharded workload (25.8 GB of host inputs per step)"
         if tri is not None:
             line["tribench_timing"] = {k_: (round(v_, 5) if isinstance(v_, float) else v_) for k_, v_ in tri.items()}
+        if blkq1 is not None:
+            line["blkq_1"] = blkq1
+        if triton_ref is not None:
+            line["triton_reference"] = triton_ref
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
