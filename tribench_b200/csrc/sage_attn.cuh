@@ -167,6 +167,13 @@ struct AttnCfg {
 #else
   static constexpr int EMU = (D == 64 && !FLASH) ? 8 : 12;
 #endif
+  // fp16 P: exponentials as packed ex2.approx.f16x2 of the fp16-rounded argument (P comes out
+  // in the P.V operand type), row sums in fp32 of those same fp16 values
+#ifdef SAGE_EX2H
+  static constexpr bool EX2H = (PV == kPvF16);
+#else
+  static constexpr bool EX2H = false;
+#endif
 };
 
 // Bounded-wait limit sentinel codes (match SAGE_DEV_* in sage_sm100.h).
@@ -711,6 +718,12 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH, C16>::NUM_THREADS, 1
         for (int pr = 0; pr < 32; ++pr) {
           const int c = h2 * 64 + 2 * pr;
           const float2 a = ffma2(make_float2(b[c], b[c + 1]), scv, ccv);
+          if constexpr (C::EX2H) {
+            const uint32_t ph = ex2_f16x2(cvt_f16x2(a));
+            acc[pr & 3] = add_f32_f16x2(acc[pr & 3], ph);
+            pk[pr] = ph;
+            continue;
+          }
           float2 e;
           if ((c % 32) >= 32 - C::EMU) {
             e = exp2_poly2(a);
