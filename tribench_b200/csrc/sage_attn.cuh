@@ -94,11 +94,15 @@ struct AttnCfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + QT * Q_TILE;
   static constexpr int OFF_V = OFF_K + NS * K_TILE;
-  // D = 64 INT8 scores start from a bias block: S = 0x4B400000 + s directly (see issue_qk).
-  // The copy shape follows the measurements: with 16-bit P.V, whose MMAs keep the tensor pipe
-  // busier, the broadcasting 32x128b.warpx4 copy (s8k_d64 1.618 -> 1.587 ms; 128x256b made it
-  // slower); with FP8 P.V the 128x256b copy (C4 1.807 -> 1.772 ms).
-  static constexpr bool PRE_BIAS = (D == 64) && !QK_F16;
+  // INT8 scores start from a bias block: S = 0x4B400000 + s directly (see issue_qk), so the
+  // softmax needs no integer add per score. The copy shape follows the measurements: with 16-bit
+  // P.V, whose MMAs keep the tensor pipe busier, the broadcasting 32x128b.warpx4 copy (s8k_d64
+  // 1.618 -> 1.587 ms; 128x256b made it slower); with FP8 P.V the 128x256b copy (C4 1.807 ->
+  // 1.772 ms). At D = 128 (same-call A/B against the integer add: H8K 1.817-1.821 -> 1.742-1.789
+  // ms, C2 0.978 -> 0.966 ms, bit-identical output) the copy into S_t(j+1) is issued after
+  // P.V_t(j), which reads P_t(j) from the upper columns of S_t: like the QK^T MMA that follows it,
+  // the copy executes in issue order in the tensor pipe, after P.V_t(j).
+  static constexpr bool PRE_BIAS = !QK_F16;
   static constexpr int OFF_BIAS = OFF_V + NS * V_TILE;          // 4 KB of 0x4B400000 words
   static constexpr int OFF_BAR = OFF_BIAS + (PRE_BIAS ? 4096 : 0);
   // q, kfull/vfull/kvempty per stage, sfull/phalf/pfull/odone/sload/pvdone per query tile
@@ -167,13 +171,6 @@ struct AttnCfg {
 #else
   static constexpr int EMU = (D == 64 && !FLASH) ? 8 : 12;
 #endif
-  // fp16 P: exponentials as packed ex2.approx.f16x2 of the fp16-rounded argument (P comes out
-  // in the P.V operand type), row sums in fp32 of those same fp16 values
-#ifdef SAGE_EX2H
-  static constexpr bool EX2H = (PV == kPvF16);
-#else
-  static constexpr bool EX2H = false;
-#endif
 };
 
 // Bounded-wait limit sentinel codes (match SAGE_DEV_* in sage_sm100.h).
@@ -182,7 +179,7 @@ enum : int { kDevTimeoutProducer = 1, kDevTimeoutMma = 2, kDevTimeoutSoftmax = 4
 // QK^T of one query tile against one K tile: S (TMEM) = Q (smem) . K (smem)^T. With PRE_BIAS
 // the S columns are first filled with the word 0x4B400000 (tcgen05.cp from a constant block) and
 // the MMA accumulates onto it, so each int32 score s arrives as the bit pattern of the float
-// 1.5 * 2^23 + s (|s| <= 127^2 * 64 < 2^22), which softmax uses without an integer add.
+// 1.5 * 2^23 + s (|s| <= 127^2 * 128 < 2^22), which softmax uses without an integer add.
 template <class C>
 __device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint32_t k_tile, uint32_t bias_addr) {
   if constexpr (C::PRE_BIAS) {
@@ -718,12 +715,6 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH, C16>::NUM_THREADS, 1
         for (int pr = 0; pr < 32; ++pr) {
           const int c = h2 * 64 + 2 * pr;
           const float2 a = ffma2(make_float2(b[c], b[c + 1]), scv, ccv);
-          if constexpr (C::EX2H) {
-            const uint32_t ph = ex2_f16x2(cvt_f16x2(a));
-            acc[pr & 3] = add_f32_f16x2(acc[pr & 3], ph);
-            pk[pr] = ph;
-            continue;
-          }
           float2 e;
           if ((c % 32) >= 32 - C::EMU) {
             e = exp2_poly2(a);

@@ -372,27 +372,6 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
                      __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
-// Two fp32 values rounded to an fp16 pair: x in the low half, y in the high half.
-__device__ __forceinline__ uint32_t cvt_f16x2(float2 a) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(a.y), "f"(a.x));
-  return r;
-}
-// 2^x of both halves of an fp16 pair on MUFU (one instruction for two exponentials).
-__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t r;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
-  return r;
-}
-// acc + (low, high halves of the fp16 pair h), each sum in fp32 (mixed-precision add).
-__device__ __forceinline__ float2 add_f32_f16x2(float2 acc, uint32_t h) {
-  float2 r;
-  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-      "add.rn.f32.f16 %0, lo, %3;\n\tadd.rn.f32.f16 %1, hi, %4;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "r"(h), "f"(acc.x), "f"(acc.y));
-  return r;
-}
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
