@@ -10,8 +10,11 @@ smoothed K, fp16 P.V — the S=8K D=128 configuration the headline metric is quo
 
 Multi-GPU (torchrun, one process per GPU): the (batch x head) grid is partitioned across the
 ranks and a step ends when the whole output is assembled on rank 0 — the north star's only
-collective, the final output gather: every rank computes its heads in --waves waves and sends
-each finished wave to rank 0 (NCCL point to point) while it computes the next one. The default
+collective, the final output gather. By default (--gather peer) rank 0's output buffer is mapped
+into every rank (CUDA IPC, NVLink peer access) and each rank's attention kernel stores its rows
+straight into it from the epilogue, so the gather is the kernels' own output stores; --gather
+nccl instead sends each finished wave of heads to rank 0 point to point while computing the
+next. The default
 workloads scale weakly (the global batch at N ranks is N times the 1-GPU batch, so N=1 is the
 1-GPU line exactly, with no gather); the sharded long-context workload "c5" (B=16, H=64, S=32K,
 causal) scales strongly (its fixed 1024-head grid is split). value = total ops of all ranks /
@@ -68,8 +71,11 @@ def parse():
     ap.add_argument("--e2e-chunks", type=int, default=16, help="head chunks of the host pipeline (e2e)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: output gather by peer stores from the attention epilogue into rank 0's "
+                         "IPC-mapped buffer (peer), or NCCL point to point per finished wave (nccl)")
     ap.add_argument("--waves", type=int, default=None,
-                    help="head waves per rank when gathering (default: 8 for c5, 4 otherwise)")
+                    help="head waves per rank (default 1; with --gather nccl: 8 for c5, 4 otherwise)")
     ap.add_argument("--no-triton-reference", action="store_true",
                     help="skip timing the reference's Triton kernel (baseline/_ref) at N=1")
     ap.add_argument("--no-blkq1", action="store_true", help="skip the per-token (blkq=1) side measurement")
@@ -548,10 +554,20 @@ def main():
     inp = tb.make_inputs(case, dev, seed=case["seed"], dtype=case["dtype"], heads=(lo, hi))
     q, k, v = inp["q"], inp["k"], inp["v"]
     causal, pv = case["causal"], case["pv"]
-    if strong:
-        n_waves = args.waves or 8
+    peer, gather_note = None, None
+    if gather and args.gather == "peer":
+        # the whole output on rank 0, mapped into every rank: the kernels store into it directly
+        try:
+            peer = shard.PeerOutput((1, nh_total, S, D), q.dtype, 0, dev)
+        except Exception as e:  # no IPC / peer access: the NCCL gather instead
+            gather_note = f"peer mapping unavailable ({type(e).__name__}: {e}); NCCL gather used"
+    nccl_gather = gather and peer is None
+    if args.waves:
+        n_waves = args.waves
+    elif nccl_gather:
+        n_waves = 8 if strong else 4
     else:
-        n_waves = (args.waves or 4) if gather else 1
+        n_waves = 1 if not strong or gather else 8
     waves = shard.wave_ranges(lo, hi, n_waves)
 
     def make_plans(blkq=128):
@@ -565,7 +581,11 @@ def main():
     plans = make_plans()
     plan = plans[waves[0][1] - waves[0][0]]
     full = None
-    if gather and rank == 0:
+    if peer is not None:
+        # every rank's slice of rank 0's buffer (local on rank 0, a peer mapping elsewhere)
+        full = peer.tensor
+        o = full[:, lo:hi]
+    elif gather and rank == 0:
         # the whole job's output lives on rank 0; its own heads are computed straight into it
         full = torch.empty((1, nh_total, S, D), dtype=q.dtype, device=dev)
         o = full[:, lo:hi]
@@ -597,8 +617,8 @@ def main():
         if ev is not None:
             ev[2].record(stream)
 
-    # one step = every wave of this rank, then (N > 1) the output gather to rank 0, each wave
-    # sent while the next one is computed
+    # one step = every wave of this rank; N > 1: with peer stores the output is then on rank 0
+    # already, with the NCCL gather each wave is sent while the next one is computed
     def step(wave_events=None, pls=None):
         if flush is not None:
             flush.zero_()
@@ -607,7 +627,7 @@ def main():
         def compute(a, b):
             wave(a, b, next(it) if it is not None else None, pls)
 
-        if gather:
+        if nccl_gather:
             shard.gather_to(0, o, sd, full, waves=n_waves, compute=compute, timeout_s=300.0)
         else:
             for (a, b) in waves:
@@ -752,9 +772,15 @@ def main():
         if gather:
             line["gather"] = {"dst_rank": 0,
                               "bytes_received_per_step": (nh_total - (hi - lo)) * S * D * q.element_size(),
-                              "overlapped": "each rank sends wave w while computing wave w+1",
+                              "method": "NCCL point to point per wave" if nccl_gather else
+                              "peer stores: each rank's attention epilogue writes its rows into rank 0's "
+                              "output over NVLink (CUDA IPC mapping), no collective",
+                              "overlapped": "each rank sends wave w while computing wave w+1" if nccl_gather else
+                              "the stores are the kernel's own output stores, spread over its run",
                               "compute_ms_per_step_max_over_ranks": round(compute_ms_max, 4),
                               "exposed_ms_per_step": round(total_ms / args.steps - compute_ms_max, 4)}
+        if gather_note:
+            line["gather"]["note"] = gather_note
         if strong:
             line["e2e_note"] = "not measured for the sharded workload (25.8 GB of host inputs per step)"
         if tri is not None:
@@ -767,6 +793,8 @@ def main():
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     del plan, plans, q, k, v, o, full
+    if peer is not None:
+        peer.close()
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()

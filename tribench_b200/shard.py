@@ -3,9 +3,14 @@
 Every (batch, head) slab is independent (the reference's grid, triton_impl.py:186, is over
 query blocks x heads x batches; nothing crosses heads), so ranks take contiguous ranges of the
 flattened (b*H + h) index and compute them with no collective. The only data movement, when a
-caller wants the whole output on one rank, is the final gather: each rank sends its finished
-head ranges to the destination point-to-point, wave by wave, so that the transfer of wave w
-overlaps the computation of wave w+1.
+caller wants the whole output on one rank, is the final gather, in one of two forms:
+  * PeerOutput: the destination's output buffer is mapped into every rank (CUDA IPC with peer
+    access over NVLink), and each rank's attention kernel stores its heads' rows straight into
+    it from its epilogue — the transfer is the kernel's own output stores, spread over its
+    whole run, with no collective and no extra pass;
+  * gather_to: each rank sends its finished head ranges to the destination point to point
+    (NCCL on GPUs, gloo on CPUs), wave by wave, so that the transfer of wave w overlaps the
+    computation of wave w+1.
 """
 from __future__ import annotations
 
@@ -99,3 +104,76 @@ def gather_to(dst: int, out_local: torch.Tensor, shard: Shard, full: torch.Tenso
     for q in reqs:
         q.wait(limit)
     return full if rank == dst else None
+
+
+class _CudaArray:
+    """A bare device pointer presented through the CUDA array interface (bytes, no ownership)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerOutput:
+    """The whole job's output `[*shape]` of `dtype`, resident on rank `dst`'s GPU and mapped into
+    every rank of `group`: ``.tensor`` views it on every rank (on rank `dst` it is local memory;
+    elsewhere a peer mapping of it, opened with CUDA IPC and NVLink peer access), so a rank that
+    computes into its slice of ``.tensor`` stores its rows directly into rank `dst`'s memory.
+
+    Collective: every rank of the group constructs it (one broadcast of the 64-byte IPC handle).
+    ``close()`` is collective too: the mappings are closed before the owner frees the buffer.
+    Rank `dst` allocates the buffer with cudaMalloc (outside torch's caching allocator, so the
+    IPC handle describes exactly this buffer). Stores from other ranks become visible on `dst`
+    once their kernels complete; a barrier after those kernels (e.g. the one that ends a timed
+    region) orders them before `dst` reads the output."""
+
+    def __init__(self, shape, dtype: torch.dtype, dst: int, device, group=None):
+        import math
+
+        import torch.distributed as dist
+        from cuda.bindings import runtime as rt
+
+        self._rt, self._group, self._dst = rt, group, dst
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        self.nbytes = math.prod(shape) * torch.empty((), dtype=dtype).element_size()
+        self._ptr = None
+
+        def ok(res, what):
+            err = res[0] if isinstance(res, tuple) else res
+            if err != rt.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"{what} failed: {err}")
+            return res[1] if isinstance(res, tuple) and len(res) > 1 else None
+
+        self._ok = ok
+        with torch.cuda.device(self.device):
+            if self.rank == dst:
+                self._ptr = int(ok(rt.cudaMalloc(self.nbytes), "cudaMalloc"))
+                handle = ok(rt.cudaIpcGetMemHandle(self._ptr), "cudaIpcGetMemHandle")
+                payload = [bytes(handle.reserved)]
+            else:
+                payload = [None]
+            dist.broadcast_object_list(payload, src=dst, group=group, device=self.device)
+            if self.rank != dst:
+                handle = rt.cudaIpcMemHandle_t()
+                handle.reserved = payload[0]
+                self._ptr = int(ok(rt.cudaIpcOpenMemHandle(handle, rt.cudaIpcMemLazyEnablePeerAccess),
+                                   "cudaIpcOpenMemHandle"))
+        self.tensor = torch.as_tensor(_CudaArray(self._ptr, self.nbytes)).view(dtype).view(*shape)
+
+    def close(self):
+        import torch.distributed as dist
+
+        if self._ptr is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self._group)
+        with torch.cuda.device(self.device):
+            if self.rank != self._dst:
+                self._ok(self._rt.cudaIpcCloseMemHandle(self._ptr), "cudaIpcCloseMemHandle")
+        dist.barrier(group=self._group)
+        if self.rank == self._dst:
+            with torch.cuda.device(self.device):
+                self._ok(self._rt.cudaFree(self._ptr), "cudaFree")
+        self.tensor = None
+        self._ptr = None
