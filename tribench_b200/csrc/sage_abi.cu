@@ -480,6 +480,20 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
 // valid stride serves; this one covers the whole tensor.
 int64_t packed_batch_stride(const int64_t* s, int64_t H, int64_t rows) { return std::max(s[1] * H, s[2] * rows); }
 
+// Whether o is anything but memory of the current device (a peer GPU's memory mapped here for a
+// multi-GPU gather, managed or host memory): the attention epilogue then stages its rows and
+// stores whole lines. A failed query counts as remote (the staged path is correct for any o).
+bool out_is_remote(const void* o) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, o) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return true;
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return true;
+  return a.type != cudaMemoryTypeDevice || a.device != dev;
+}
+
 // Sets the tensor-shape fields that dense and packed batches share; rows / batch extents of the
 // tensor maps come from here too.
 void set_seq_params(sage::AttnParams& p, const Varlen* vl, const int64_t* os, int64_t B, int64_t Hq, int64_t Hkv,
@@ -490,6 +504,7 @@ void set_seq_params(sage::AttnParams& p, const Varlen* vl, const int64_t* os, in
   p.nqb = (int)cdiv(Sq, 128); p.nkb = (int)cdiv(Skv, 64);
   p.qblk_shift = 7;
   p.causal = causal ? 1 : 0;
+  p.o_stage = out_is_remote(p.o) ? 1 : 0;
   p.n_m_ctas = (int)cdiv(Sq, 256);
   p.wait_limit_ns = wait_limit_ns();
   if (vl) { p.cu_q = vl->cu_q; p.cu_k = vl->cu_k; p.q_tokens = (int)vl->q_tokens; p.k_tokens = (int)vl->k_tokens; }

@@ -59,6 +59,7 @@ struct AttnParams {
   const int* cu_k;
   int q_tokens, k_tokens;
   int causal;
+  int o_stage;               // 1: o is not this GPU's own memory (e.g. a peer mapping): line-coalesced stores
   int n_m_ctas;              // CTAs along the query axis
   unsigned long long wait_limit_ns;
   float qk_scale;            // FLASH only: sm_scale * log2(e)
@@ -113,11 +114,16 @@ struct AttnCfg {
   // (16 passes x 4 warps) and the 128 row scales
   static constexpr int OFF_QFINE = OFF_QRED + 16 * QT;
   static constexpr int QFINE_BYTES = (16 * 4 + 128) * 4;
-  static constexpr int SMEM_USED = OFF_QFINE + QFINE_BYTES * QT;
+  // epilogue staging: per tile 64 output rows (half the tile) at a time, so that the copy-out
+  // writes whole lines (consecutive threads, consecutive 16-byte pieces)
+  static constexpr int OFF_OST = (OFF_QFINE + QFINE_BYTES * QT + 127) / 128 * 128;
+  static constexpr int OST_BYTES = 64 * D * 2;
+  static constexpr int SMEM_USED = OFF_OST + OST_BYTES * QT;
   // Pad to > half of the SM's shared memory so that exactly one CTA is resident per SM:
   // each CTA allocates all 512 TMEM columns when QT == 2.
   static constexpr int SMEM_MIN = (QT == 2) ? 118 * 1024 : 0;
   static constexpr int SMEM_BYTES = 1024 + (SMEM_USED > SMEM_MIN ? SMEM_USED : SMEM_MIN);
+  static_assert(SMEM_BYTES <= 227 * 1024, "dynamic shared memory per CTA");
   // softmax warpgroups, then one warpgroup with the producer, the MMA issuer and two idle warps
   static constexpr int NUM_THREADS = 32 * (4 * QT + 4);
   // Launch allocation 168 registers/thread (3 warps per SM sub-partition); the softmax
@@ -216,6 +222,17 @@ __device__ __forceinline__ void issue_qk(uint32_t s_tmem, uint32_t q_tile, uint3
 __device__ __forceinline__ void warpgroup_sync(int t) {
   if (t == 0) asm volatile("bar.sync 3, 128;" ::: "memory");
   else asm volatile("bar.sync 4, 128;" ::: "memory");
+}
+// The same barrier, returning whether v holds for all 128 threads (bar.red.and).
+__device__ __forceinline__ bool warpgroup_and(int t, bool v) {
+  uint32_t r;
+  if (t == 0)
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 3, 128, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}" : "=r"(r) : "r"(v ? 1u : 0u) : "memory");
+  else
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 4, 128, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}" : "=r"(r) : "r"(v ? 1u : 0u) : "memory");
+  return r != 0;
 }
 
 // fused_q_tile with Q scale blocks of 2^qblk_shift < 128 rows (1 = per token, 16, 32, 64). Pass
@@ -775,35 +792,85 @@ __global__ void __launch_bounds__(AttnCfg<D, PV, QT, FLASH, C16>::NUM_THREADS, 1
     }
     SAGE_T_MARK(5)
     // ---------------------------------------------------------- epilogue
+    // O = acc / l in the output type. Into this GPU's own memory each thread stores its row
+    // directly. Into other memory (p.o_stage: a peer-mapped output of a multi-GPU gather) each
+    // half of the tile (64 rows, two warps' TMEM lanes) goes through shared memory and out with
+    // whole-line stores: thread i writes 16-byte piece i of the half's rows, so a warp's store
+    // covers 512 contiguous bytes of a head's rows instead of 32 rows' separate pieces, which
+    // NVLink carries far more efficiently. Row r's 16-byte piece c sits in the stage at piece
+    // c ^ (r mod PR) (PR pieces per row) against bank conflicts. On that path all four warps of
+    // the warpgroup execute every barrier, and whether the tile stores anything is one
+    // warpgroup-wide decision (bar.red.and), so a warp whose wait gave up cannot leave the
+    // others waiting.
     const bool valid = row < Sq;
-    char* orow_ptr = reinterpret_cast<char*>(p.o) +
-                     ((int64_t)sq.batch * p.o_sb + (int64_t)h * p.o_sh + (int64_t)(sq.base + row) * p.o_ss) * 2;
-    if (ok && n > 0 &&
-        __all_sync(0xffffffffu, mbar_wait(bar_odone + t, 0, abort_flag, kDevTimeoutEpilogue, p.wait_limit_ns))) {
+    const int64_t o_row0 = (int64_t)sq.batch * p.o_sb + (int64_t)h * p.o_sh + (int64_t)(sq.base + r0) * p.o_ss;
+    char* orow_ptr = reinterpret_cast<char*>(p.o) + (o_row0 + (int64_t)row_in_tile * p.o_ss) * 2;
+    const float inv_l = 1.0f / l_run;
+    const float* vsp = p.v_scale + ((size_t)b * p.Hkv + hkv) * D;
+    // output columns [c0, c0 + 32) of this thread's row, scaled and packed to 16-bit pairs
+    auto out32 = [&](int c0, uint32_t (&packed)[16]) {
+      uint32_t orow[32];
+      tmem_ld32_sync(o_tmem + c0, orow);
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        float a = __uint_as_float(orow[c]) * inv_l;
+        float z = __uint_as_float(orow[c + 1]) * inv_l;
+        if constexpr (PV == kPvE4M3) {
+          a *= vsp[c0 + c];
+          z *= vsp[c0 + c + 1];
+        }
+        if constexpr (OBF16) {
+          __nv_bfloat162 v2 = __floats2bfloat162_rn(a, z);
+          packed[c / 2] = *reinterpret_cast<uint32_t*>(&v2);
+        } else {
+          __half2 v2 = __floats2half2_rn(a, z);
+          packed[c / 2] = *reinterpret_cast<uint32_t*>(&v2);
+        }
+      }
+    };
+    if (n > 0 && p.o_stage) {  // uniform over the warpgroup
+      const bool mine = ok && __all_sync(0xffffffffu, mbar_wait(bar_odone + t, 0, abort_flag, kDevTimeoutEpilogue,
+                                                               p.wait_limit_ns));
+      const bool store = warpgroup_and(t, mine);
       tc_fence_after();
-      const float inv_l = 1.0f / l_run;
-      const float* vsp = p.v_scale + ((size_t)b * p.Hkv + hkv) * D;
+      constexpr int PR = D / 8;  // 16-byte pieces per output row
+      uint4* stage = reinterpret_cast<uint4*>(smem + C::OFF_OST + t * C::OST_BYTES);
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t orow[32];
-        tmem_ld32_sync(o_tmem + c0, orow);
-        uint32_t packed[16];
+      for (int half = 0; half < 2; ++half) {
+        if (store && (warp % 4) / 2 == half) {
+          const int lr = row_in_tile - 64 * half;
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float a = __uint_as_float(orow[c]) * inv_l;
-          float z = __uint_as_float(orow[c + 1]) * inv_l;
-          if constexpr (PV == kPvE4M3) {
-            a *= vsp[c0 + c];
-            z *= vsp[c0 + c + 1];
-          }
-          if constexpr (OBF16) {
-            __nv_bfloat162 v2 = __floats2bfloat162_rn(a, z);
-            packed[c / 2] = *reinterpret_cast<uint32_t*>(&v2);
-          } else {
-            __half2 v2 = __floats2half2_rn(a, z);
-            packed[c / 2] = *reinterpret_cast<uint32_t*>(&v2);
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t packed[16];
+            out32(c0, packed);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int piece = c0 / 8 + v;
+              stage[lr * PR + (piece ^ (lr % PR))] =
+                  make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            }
           }
         }
+        warpgroup_sync(t);
+        if (store) {
+#pragma unroll
+          for (int i = 0; i < 64 * PR / 128; ++i) {
+            const int idx = i * 128 + row_in_tile;
+            const int lr = idx / PR, piece = idx % PR, r = 64 * half + lr;
+            if (r0 + r < Sq)
+              *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.o) + (o_row0 + (int64_t)r * p.o_ss) * 2 + piece * 16) =
+                  stage[lr * PR + (piece ^ (lr % PR))];
+          }
+        }
+        warpgroup_sync(t);  // the stage is free for the next half
+      }
+    } else if (ok && n > 0 &&
+               __all_sync(0xffffffffu, mbar_wait(bar_odone + t, 0, abort_flag, kDevTimeoutEpilogue, p.wait_limit_ns))) {
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t packed[16];
+        out32(c0, packed);
         if (valid) {
           uint4* dst = reinterpret_cast<uint4*>(orow_ptr + c0 * 2);
 #pragma unroll
