@@ -29,6 +29,13 @@
  * intermediate or the workspace, or overlap q other than as the identical view (same base
  * pointer and strides; in place, o = q, is allowed). The check compares the byte ranges the
  * tensors span, so an o interleaved with k or v inside one packed buffer is rejected too.
+ *
+ * Output placement: o may be memory of the calling GPU, another GPU's memory mapped into
+ * this one (CUDA IPC or peer access over NVLink: each GPU of a multi-GPU job writes its rows
+ * straight into one GPU's output buffer), or mapped pinned host memory. When o is not memory of
+ * the current device (cudaPointerGetAttributes), the attention epilogue stages each half tile
+ * in shared memory and writes whole 128-byte lines, which NVLink carries far better than one
+ * row's 16-byte pieces; results are bit-identical either way.
  */
 #ifndef SAGE_SM100_H_
 #define SAGE_SM100_H_
