@@ -69,7 +69,8 @@ def test_flash_staged_store_equals_direct_store(D):
 
 @pytest.mark.parametrize("D,causal", [(128, True), (64, False)])
 def test_varlen_staged_store_equals_direct_store(D, causal):
-    lens_q, lens_k = [300, 0, 1, 517], [290, 40, 128, 700]
+    lens_q = [300, 0, 1, 517]
+    lens_k = lens_q if causal else [290, 40, 128, 700]  # causal: equal lengths per sequence
     cu_q = torch.tensor([0] + torch.tensor(lens_q).cumsum(0).tolist(), dtype=torch.int32, device=DEV)
     cu_k = torch.tensor([0] + torch.tensor(lens_k).cumsum(0).tolist(), dtype=torch.int32, device=DEV)
     Hq, Hkv = 4, 2
