@@ -10,11 +10,13 @@ smoothed K, fp16 P.V — the S=8K D=128 configuration the headline metric is quo
 
 Multi-GPU (torchrun, one process per GPU): the (batch x head) grid is partitioned across the
 ranks and a step ends when the whole output is assembled on rank 0 — the north star's only
-collective, the final output gather. By default (--gather peer) rank 0's output buffer is mapped
-into every rank (CUDA IPC, NVLink peer access) and each rank's attention kernel stores its rows
-straight into it from the epilogue, so the gather is the kernels' own output stores; --gather
-nccl instead sends each finished wave of heads to rank 0 point to point while computing the
-next. The default
+collective, the final output gather. Rank 0's output buffer is mapped into every rank (CUDA
+IPC, NVLink peer access). By default (--gather copy) each rank computes its heads in 8 waves
+that alternate over two compute streams (consecutive waves overlap, so no SM idles at a wave's
+end) and copies every finished wave into the mapping with the copy engine while the next waves
+compute; --gather peer lets the attention epilogues store straight into the mapping (SM stores
+into another GPU's memory reach only ~170 GB/s at the destination); --gather nccl sends each
+finished wave to rank 0 point to point while computing the next. The default
 workloads scale weakly (the global batch at N ranks is N times the 1-GPU batch, so N=1 is the
 1-GPU line exactly, with no gather); the sharded long-context workload "c5" (B=16, H=64, S=32K,
 causal) scales strongly (its fixed 1024-head grid is split). value = total ops of all ranks /
@@ -71,9 +73,10 @@ def parse():
     ap.add_argument("--e2e-chunks", type=int, default=16, help="head chunks of the host pipeline (e2e)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
-                    help="N > 1: output gather by peer stores from the attention epilogue into rank 0's "
-                         "IPC-mapped buffer (peer), or NCCL point to point per finished wave (nccl)")
+    ap.add_argument("--gather", default="copy", choices=["copy", "peer", "nccl"],
+                    help="N > 1: output gather into rank 0's IPC-mapped buffer by copy-engine copies of each "
+                         "finished wave, waves on two overlapping compute streams (copy); by peer stores from "
+                         "the attention epilogue (peer); or NCCL point to point per finished wave (nccl)")
     ap.add_argument("--waves", type=int, default=None,
                     help="head waves per rank (default 1; with --gather nccl: 8 for c5, 4 otherwise)")
     ap.add_argument("--no-triton-reference", action="store_true",
@@ -555,17 +558,20 @@ def main():
     q, k, v = inp["q"], inp["k"], inp["v"]
     causal, pv = case["causal"], case["pv"]
     peer, gather_note = None, None
-    if gather and args.gather == "peer":
+    if gather and args.gather in ("copy", "peer"):
         # the whole output on rank 0, mapped into every rank: the kernels store into it directly
         try:
             peer = shard.PeerOutput((1, nh_total, S, D), q.dtype, 0, dev)
         except Exception as e:  # no IPC / peer access: the NCCL gather instead
             gather_note = f"peer mapping unavailable ({type(e).__name__}: {e}); NCCL gather used"
     nccl_gather = gather and peer is None
+    copy_gather = peer is not None and args.gather == "copy"
     if args.waves:
         n_waves = args.waves
     elif nccl_gather:
         n_waves = 8 if strong else 4
+    elif copy_gather:
+        n_waves = 8
     else:
         n_waves = 1 if not strong or gather else 8
     waves = shard.wave_ranges(lo, hi, n_waves)
@@ -579,9 +585,15 @@ def main():
         return out
 
     plans = make_plans()
+    plans_alt = make_plans() if copy_gather else None  # the second compute stream's buffers
     plan = plans[waves[0][1] - waves[0][0]]
     full = None
-    if peer is not None:
+    if copy_gather:
+        # rank 0 computes straight into its slice of the mapped buffer; the others compute
+        # locally and the copy engine moves each finished wave into the mapping
+        full = peer.tensor
+        o = full[:, lo:hi] if rank == 0 else torch.empty_like(q)
+    elif peer is not None:
         # every rank's slice of rank 0's buffer (local on rank 0, a peer mapping elsewhere)
         full = peer.tensor
         o = full[:, lo:hi]
@@ -608,17 +620,22 @@ def main():
     def wave(a, b, ev=None, pls=None):
         i, j = a - lo, b - lo
         pl = (pls or plans)[j - i]
+        cur = torch.cuda.current_stream(dev)
         if ev is not None:
-            ev[0].record(stream)
+            ev[0].record(cur)
         pl.prepass(q[:, i:j], k[:, i:j], v[:, i:j])
         if ev is not None:
-            ev[1].record(stream)
+            ev[1].record(cur)
         pl.attention(v[:, i:j], o[:, i:j], q=q[:, i:j])
         if ev is not None:
-            ev[2].record(stream)
+            ev[2].record(cur)
 
-    # one step = every wave of this rank; N > 1: with peer stores the output is then on rank 0
-    # already, with the NCCL gather each wave is sent while the next one is computed
+    # one step = every wave of this rank; N > 1: with the copy gather each finished wave is
+    # copied into rank 0's buffer while the next ones compute, with peer stores the output is on
+    # rank 0 already, with the NCCL gather each wave is sent while the next one is computed
+    cg = shard.CopyGather(peer, lo, o) if copy_gather else None
+    cg_events = []
+
     def step(wave_events=None, pls=None):
         if flush is not None:
             flush.zero_()
@@ -627,7 +644,12 @@ def main():
         def compute(a, b):
             wave(a, b, next(it) if it is not None else None, pls)
 
-        if nccl_gather:
+        if cg is not None:
+            evs_ = cg.step(waves, lambda a, b, slot: wave(a, b, next(it) if it is not None else None,
+                                                          plans if slot == 0 else plans_alt))
+            if wave_events is not None:
+                cg_events.append(evs_)
+        elif nccl_gather:
             shard.gather_to(0, o, sd, full, waves=n_waves, compute=compute, timeout_s=300.0)
         else:
             for (a, b) in waves:
@@ -662,7 +684,11 @@ def main():
     attn_ms = [sum(w[1].elapsed_time(w[2]) for w in evs[i]) for i in range(args.steps)]
     pre_ms = [sum(w[0].elapsed_time(w[1]) for w in evs[i]) for i in range(args.steps)]
     status = tb.device_status(dev)
-    compute_ms = statistics.mean(a + b for a, b in zip(attn_ms, pre_ms))
+    if cg is not None:
+        # waves overlap on two streams: this rank's compute span is start -> the later stream end
+        compute_ms = statistics.mean(max(st.elapsed_time(em), st.elapsed_time(ea)) for st, em, ea, _ in cg_events)
+    else:
+        compute_ms = statistics.mean(a + b for a, b in zip(attn_ms, pre_ms))
     if pg is not None:
         # rank 0 stores its own rows into local memory: its compute time is the step without
         # any gather traffic of its own, the yardstick for what the gather costs
@@ -754,7 +780,9 @@ def main():
                          "peak_sustained_mixed": rl.get("mixed_sustained"),
                          "frac_vs_sustained_mixed": round(achieved / rl["mixed_sustained"], 4)
                          if rl.get("mixed_sustained") else None,
-                         "attn_ms": round(attn_avg, 4), "prepass_ms": round(statistics.mean(pre_ms), 4)},
+                         "attn_ms": round(attn_avg, 4), "prepass_ms": round(statistics.mean(pre_ms), 4),
+                         **({"note": "waves overlap on two streams: attn_ms sums per-wave kernel durations that "
+                                     "overlap one another, so achieved is a lower bound"} if cg is not None else {})},
             "prepass_roofline": {"bound": "hbm", "achieved": round(tb.prepass_bytes(dict(case, batch_size=1,
                                  num_heads=hi - lo), fused_q=plan.fused_q) / (statistics.mean(pre_ms) * 1e-3) / 1e9, 1),
                                  "peak": peaks["hbm"], "unit": "GB/s",
@@ -775,9 +803,13 @@ def main():
             line["gather"] = {"dst_rank": 0,
                               "bytes_received_per_step": (nh_total - (hi - lo)) * S * D * q.element_size(),
                               "method": "NCCL point to point per wave" if nccl_gather else
+                              "copy engine: each rank's finished waves copied (cudaMemcpyAsync) into rank 0's "
+                              "output over NVLink (CUDA IPC mapping), no collective" if copy_gather else
                               "peer stores: each rank's attention epilogue writes its rows into rank 0's "
                               "output over NVLink (CUDA IPC mapping), no collective",
                               "overlapped": "each rank sends wave w while computing wave w+1" if nccl_gather else
+                              f"{len(waves)} waves alternating over two compute streams; wave w copied on a "
+                              "third stream while later waves compute" if copy_gather else
                               "the stores are the kernel's own output stores, spread over its run",
                               "compute_ms_per_step_rank0": round(compute_ms_r0, 4),
                               "compute_ms_per_step_max_over_ranks": round(compute_ms_max, 4),

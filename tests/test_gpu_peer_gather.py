@@ -1,10 +1,13 @@
-"""GPU, 2 ranks (skipped with fewer than 2 GPUs): the output gather by peer stores.
+"""GPU, 2 ranks (skipped with fewer than 2 GPUs): the output gathers into a mapped buffer.
 
-Rank 0's output buffer is mapped into rank 1 (shard.PeerOutput: CUDA IPC, NVLink peer access);
-each rank runs sage_run on its half of the heads with its output pointing into that buffer, so
-rank 1's attention epilogue stores straight into rank 0's memory. After a barrier, rank 0 holds
-the whole output, which must equal a single-GPU run over all heads bit for bit. A second step
-into the same buffer checks that nothing from the first leaks into it.
+Rank 0's output buffer is mapped into rank 1 (shard.PeerOutput: CUDA IPC, NVLink peer access).
+"peer": each rank runs sage_run on its half of the heads with its output pointing into that
+buffer, so rank 1's attention epilogue stores straight into rank 0's memory. "copy"
+(shard.CopyGather): each rank computes its heads in waves on two alternating streams, rank 0
+into its slice of the buffer and rank 1 into local memory, whose finished waves the copy engine
+moves into the mapping. After a barrier, rank 0 holds the whole output, which must equal a
+single-GPU run over all heads bit for bit. A second step into the same buffer checks that
+nothing from the first leaks into it.
 """
 import datetime
 import os
@@ -15,7 +18,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _rank_main(rank, world, port, case, results):
+def _rank_main(rank, world, port, case, results, mode="peer"):
     import torch.distributed as dist
 
     import tribench_b200 as tb
@@ -34,8 +37,22 @@ def _rank_main(rank, world, port, case, results):
         for seed in (case["seed"], case["seed"] + 1):
             inp = tb.make_inputs(case, dev, seed=seed, dtype="fp16", heads=(sd.lo, sd.hi))
             n = sd.heads
-            plan = tb.SagePlan(1, n, n, S, S, D, torch.float16, dev, causal=case["causal"])
-            plan.run(inp["q"], inp["k"], inp["v"], peer.tensor[:, sd.lo:sd.hi])
+            if mode == "peer":
+                plan = tb.SagePlan(1, n, n, S, S, D, torch.float16, dev, causal=case["causal"])
+                plan.run(inp["q"], inp["k"], inp["v"], peer.tensor[:, sd.lo:sd.hi])
+            else:
+                waves = shard.wave_ranges(sd.lo, sd.hi, 3)  # uneven waves: sizes 1 and 2 heads
+                out = peer.tensor[:, sd.lo:sd.hi] if rank == 0 else torch.empty_like(inp["q"])
+                plans = [{}, {}]
+
+                def compute(a, b, slot):
+                    m = b - a
+                    pl = plans[slot].setdefault(m, tb.SagePlan(1, m, m, S, S, D, torch.float16, dev,
+                                                                causal=case["causal"]))
+                    i, j = a - sd.lo, b - sd.lo
+                    pl.run(inp["q"][:, i:j], inp["k"][:, i:j], inp["v"][:, i:j], out[:, i:j])
+
+                shard.CopyGather(peer, sd.lo, out).step(waves, compute)
             torch.cuda.synchronize(dev)
             dist.barrier()
             if rank == 0:
@@ -54,15 +71,16 @@ def _rank_main(rank, world, port, case, results):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_peer_store_gather_matches_one_gpu_bit_for_bit():
+@pytest.mark.parametrize("mode", ["peer", "copy"])
+def test_mapped_output_gather_matches_one_gpu_bit_for_bit(mode):
     import torch.multiprocessing as mp
 
     case = dict(batch_size=2, num_heads=4, seq_len=1000, head_dim=128, causal=True, dist="offset",
                 k_offset_std=2.0, seed=5)
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
-    port = 29600 + os.getpid() % 200
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, case, results)) for r in range(2)]
+    port = 29600 + os.getpid() % 200 + (7 if mode == "copy" else 0)
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, case, results, mode)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(results.get(timeout=300) for _ in procs)

@@ -3,11 +3,15 @@
 Every (batch, head) slab is independent (the reference's grid, triton_impl.py:186, is over
 query blocks x heads x batches; nothing crosses heads), so ranks take contiguous ranges of the
 flattened (b*H + h) index and compute them with no collective. The only data movement, when a
-caller wants the whole output on one rank, is the final gather, in one of two forms:
-  * PeerOutput: the destination's output buffer is mapped into every rank (CUDA IPC with peer
-    access over NVLink), and each rank's attention kernel stores its heads' rows straight into
-    it from its epilogue — the transfer is the kernel's own output stores, spread over its
-    whole run, with no collective and no extra pass;
+caller wants the whole output on one rank, is the final gather, in one of three forms:
+  * CopyGather (over a PeerOutput): the destination's output buffer is mapped into every rank
+    (CUDA IPC with peer access over NVLink); each rank computes its heads in waves into its own
+    memory, on two compute streams so that consecutive waves overlap (no SM idles at a wave's
+    end), and a copy stream sends every finished wave into the mapping with the copy engine
+    (cudaMemcpyAsync, no SM involved) while the next waves compute;
+  * PeerOutput alone: each rank's attention kernel stores its heads' rows straight into the
+    mapping from its epilogue — no extra pass, but SM stores into another GPU's memory reach
+    only ~170 GB/s at the destination on B200, a quarter of what the copy engine moves;
   * gather_to: each rank sends its finished head ranges to the destination point to point
     (NCCL on GPUs, gloo on CPUs), wave by wave, so that the transfer of wave w overlaps the
     computation of wave w+1.
@@ -177,3 +181,49 @@ class PeerOutput:
                 self._ok(self._rt.cudaFree(self._ptr), "cudaFree")
         self.tensor = None
         self._ptr = None
+
+
+class CopyGather:
+    """Per-step driver of the copy-engine gather into a PeerOutput (see the module docstring).
+
+    ``step(waves, compute)`` runs ``compute(a, b, slot)`` for every head range [a, b) of this
+    rank, alternating between the caller's current stream (slot 0) and a second stream (slot 1);
+    ``compute`` launches on the current stream and uses per-slot buffers, so two waves never
+    share scratch. On ranks other than the destination each finished wave's rows,
+    ``out_local[:, a - lo : b - lo]``, are then copied into ``peer.tensor[:, a:b]`` on a copy
+    stream; the destination computes into its slice of the buffer directly (``out_local`` is
+    that slice there). Everything is joined back into the current stream before ``step``
+    returns, so an event recorded after it covers the whole step, copies included.
+
+    Returns the step's CUDA events (start, compute end per slot, copy end), for timing."""
+
+    def __init__(self, peer: "PeerOutput", lo: int, out_local: torch.Tensor):
+        self.peer, self.lo, self.out_local = peer, lo, out_local
+        self.send = peer.rank != peer._dst
+        self.alt = torch.cuda.Stream(peer.device)
+        self.copy = torch.cuda.Stream(peer.device)
+
+    def step(self, waves, compute):
+        main = torch.cuda.current_stream(self.peer.device)
+        ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+        start, end_main, end_alt, end_copy = ev(), ev(), ev(), ev()
+        start.record(main)
+        self.alt.wait_stream(main)
+        self.copy.wait_stream(main)
+        streams = (main, self.alt)
+        for w, (a, b) in enumerate(waves):
+            s = streams[w % 2]
+            with torch.cuda.stream(s):
+                compute(a, b, w % 2)
+            if self.send:
+                done = torch.cuda.Event()
+                done.record(s)
+                self.copy.wait_event(done)
+                with torch.cuda.stream(self.copy):
+                    self.peer.tensor[:, a:b].copy_(self.out_local[:, a - self.lo:b - self.lo], non_blocking=True)
+        end_main.record(main)
+        end_alt.record(self.alt)
+        end_copy.record(self.copy)
+        main.wait_stream(self.alt)
+        main.wait_stream(self.copy)
+        return start, end_main, end_alt, end_copy
