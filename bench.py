@@ -584,9 +584,12 @@ def main():
                                          blkq=blkq)
         return out
 
-    plans = make_plans()
-    plans_alt = make_plans() if copy_gather else None  # the second compute stream's buffers
-    plan = plans[waves[0][1] - waves[0][0]]
+    plans = make_plans() if not copy_gather else {}
+    # copy gather: one pre-pass over all this rank's heads, then the attention waves read its
+    # buffers (disjoint head ranges) from two streams
+    plan_all = (tb.SagePlan(1, hi - lo, hi - lo, S, S, D, q.dtype, dev, pv=pv, smooth_k=True, causal=causal)
+                if copy_gather else None)
+    plan = plan_all if copy_gather else plans[waves[0][1] - waves[0][0]]
     full = None
     if copy_gather:
         # rank 0 computes straight into its slice of the mapped buffer; the others compute
@@ -645,18 +648,34 @@ def main():
             wave(a, b, next(it) if it is not None else None, pls)
 
         if cg is not None:
-            evs_ = cg.step(waves, lambda a, b, slot: wave(a, b, next(it) if it is not None else None,
-                                                          plans if slot == 0 else plans_alt))
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record(stream)
+            plan_all.prepass(q, k, v)
+            p1.record(stream)
+
+            def attention_wave(a, b, slot):
+                ev = next(it) if it is not None else None
+                cur = torch.cuda.current_stream(dev)
+                i, j = a - lo, b - lo
+                if ev is not None:
+                    ev[0].record(cur)
+                    ev[1].record(cur)
+                plan_all.attention(v[:, i:j], o[:, i:j], q=q[:, i:j], heads=(i, j))
+                if ev is not None:
+                    ev[2].record(cur)
+
+            evs_ = cg.step(waves, attention_wave)
             if wave_events is not None:
-                cg_events.append(evs_)
+                cg_events.append((p0, p1, *evs_))
         elif nccl_gather:
             shard.gather_to(0, o, sd, full, waves=n_waves, compute=compute, timeout_s=300.0)
         else:
             for (a, b) in waves:
                 compute(a, b)
 
-    # our kernels per wave: K-stats + finalize + quantise, then attention
-    launches_per_step = 4 * len(waves)
+    # our kernels per wave: K-stats + finalize + quantise, then attention (copy gather: the
+    # three pre-pass launches once per step, one attention launch per wave)
+    launches_per_step = ((3 if plan_all.route == "fused" else 4) + len(waves)) if copy_gather else 4 * len(waves)
 
     evs = [[tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in waves] for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -686,7 +705,9 @@ def main():
     status = tb.device_status(dev)
     if cg is not None:
         # waves overlap on two streams: this rank's compute span is start -> the later stream end
-        compute_ms = statistics.mean(max(st.elapsed_time(em), st.elapsed_time(ea)) for st, em, ea, _ in cg_events)
+        compute_ms = statistics.mean(max(p0.elapsed_time(em), p0.elapsed_time(ea)) for p0, _, _, em, ea, _ in cg_events)
+        pre_ms = [p0.elapsed_time(p1) for p0, p1, *_ in cg_events]
+        step_ms = [ev[0].elapsed_time(ends[i]) for i, ev in enumerate(cg_events)]
     else:
         compute_ms = statistics.mean(a + b for a, b in zip(attn_ms, pre_ms))
     if pg is not None:

@@ -263,15 +263,31 @@ class SagePlan:
         N.check("sage_prepass", rc)
         return self.quant
 
-    def attention(self, v, out, tensor_layout="HND", q=None):
+    def attention(self, v, out, tensor_layout="HND", q=None, heads=None):
         """The attention half of run() over the prepass() results: sage_attn_fwd (route "int8"),
-        sage_attn_fwd_codes16 ("codes16") or sage_attn_fwd_fused_q ("fused", which needs ``q``)."""
-        pv = "fp8" if self.pv_mode == N.SAGE_PV_FP8 else "16bit"
-        if self.route == "int8":
-            return attn_fwd(self.quant, v, self.causal, pv=pv, out_dtype=self.dtype, tensor_layout=tensor_layout,
-                            out=out)
+        sage_attn_fwd_codes16 ("codes16") or sage_attn_fwd_fused_q ("fused", which needs ``q``).
+
+        ``heads=(i, j)`` (plans with batch 1) runs it for kv heads [i, j) only — query heads
+        [i*g, j*g) with g = heads_q / heads_kv — so that one prepass() over all heads can feed
+        several attention launches; ``v``, ``out`` and ``q`` are then that head range's tensors."""
         B, Hq, Hkv, Sq, Skv, D = self.shape
         qd = self.quant
+        codes16 = self.codes16
+        if heads is not None:
+            i, j = heads
+            if B != 1 or not (0 <= i < j <= Hkv):
+                raise ValueError(f"heads={heads}: needs a batch-1 plan and 0 <= i < j <= {Hkv}")
+            g = Hq // Hkv
+            qa, qb = i * g, j * g
+            cut = lambda t, a, b: None if t is None else t[:, a:b]  # noqa: E731
+            qd = SageQuant(cut(qd.q_int8, qa, qb), cut(qd.q_scale, qa, qb), cut(qd.k_int8, i, j),
+                           cut(qd.k_scale, i, j), None, cut(qd.v_fp8, i, j), cut(qd.v_scale, i, j), qd.blkq)
+            if codes16 is not None:
+                codes16 = (codes16[0][:, qa:qb], codes16[1][:, i:j])
+            Hq, Hkv = qb - qa, j - i
+        pv = "fp8" if self.pv_mode == N.SAGE_PV_FP8 else "16bit"
+        if self.route == "int8":
+            return attn_fwd(qd, v, self.causal, pv=pv, out_dtype=self.dtype, tensor_layout=tensor_layout, out=out)
         *_, os_ = _dims(out, tensor_layout)
         if self.pv_mode == N.SAGE_PV_FP8:
             vv, vs = qd.v_fp8, (Skv * D * Hkv, Skv * D, D)
@@ -280,10 +296,10 @@ class SagePlan:
             *_, vs = _dims(v, tensor_layout)
         lib = N.load()
         if self.route == "codes16":
-            if self.codes16 is None:
+            if codes16 is None:
                 raise ValueError("call prepass() first")
             rc = lib.sage_attn_fwd_codes16(
-                _vp(self.codes16[0]), _vp(qd.q_scale), _vp(self.codes16[1]), _vp(qd.k_scale), _vp(vv),
+                _vp(codes16[0]), _vp(qd.q_scale), _vp(codes16[1]), _vp(qd.k_scale), _vp(vv),
                 N.strides3(*vs), _vp(qd.v_scale), _vp(out), N.strides3(*os_), _DTYPES[self.dtype], self.pv_mode,
                 int(self.causal), self.qflag, B, Hq, Hkv, Sq, Skv, D, _stream_ptr(self.device))
             N.check("sage_attn_fwd_codes16", rc)
