@@ -80,9 +80,6 @@ def parse():
     ap.add_argument("--waves", type=int, default=None,
                     help="head waves per rank (default 1; with --gather copy: 8; with --gather nccl: 8 for c5, "
                          "4 otherwise)")
-    ap.add_argument("--taper", action=argparse.BooleanOptionalAction, default=True,
-                    help="--gather copy: split the last wave into halving pieces (8 heads -> 4, 2, 1, 1) so "
-                         "that one head's copy is left after the computation ends")
     ap.add_argument("--no-triton-reference", action="store_true",
                     help="skip timing the reference's Triton kernel (baseline/_ref) at N=1")
     ap.add_argument("--no-blkq1", action="store_true", help="skip the per-token (blkq=1) side measurement")
@@ -578,7 +575,7 @@ def main():
         n_waves = 8
     else:
         n_waves = 1 if not strong or gather else 8
-    waves = shard.wave_ranges(lo, hi, n_waves, taper=copy_gather and args.taper)
+    waves = shard.wave_ranges(lo, hi, n_waves)
 
     def make_plans(blkq=128):
         out = {}

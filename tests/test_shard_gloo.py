@@ -103,17 +103,6 @@ def test_wave_ranges():
     assert sh.wave_ranges(0, 2, 5) == [(0, 1), (1, 2)]
 
 
-def test_wave_ranges_taper():
-    # the last wave splits into halving pieces; the ranges still tile [lo, hi) in order
-    assert sh.wave_ranges(0, 64, 8, taper=True)[-5:] == [(48, 56), (56, 60), (60, 62), (62, 63), (63, 64)]
-    assert sh.wave_ranges(3, 10, 3, taper=True) == [(3, 5), (5, 7), (7, 9), (9, 10)]
-    assert sh.wave_ranges(0, 5, 1, taper=True) == [(0, 5)]
-    for lo, hi, w in [(0, 64, 8), (7, 135, 8), (0, 3, 8), (5, 6, 4)]:
-        r = sh.wave_ranges(lo, hi, w, taper=True)
-        assert r[0][0] == lo and r[-1][1] == hi and all(a < b for a, b in r)
-        assert all(r[i][1] == r[i + 1][0] for i in range(len(r) - 1))
-
-
 def test_gather_world2_matches_single_process():
     out = _run("ok")
     assert out[0] == ("ok", True), out

@@ -32,21 +32,10 @@ def head_range(rank: int, world: int, total: int) -> tuple[int, int]:
     return rank * total // world, (rank + 1) * total // world
 
 
-def wave_ranges(lo: int, hi: int, waves: int, taper: bool = False) -> list[tuple[int, int]]:
-    """[lo, hi) in `waves` near-equal consecutive ranges. With `taper` the last range is split
-    again into halving pieces (8 heads -> 4, 2, 1, 1), so that what is left to send after the
-    computation ends is one head, not a whole wave."""
+def wave_ranges(lo: int, hi: int, waves: int) -> list[tuple[int, int]]:
     n = hi - lo
     waves = max(1, min(waves, n)) if n > 0 else 1
-    out = [(lo + w * n // waves, lo + (w + 1) * n // waves) for w in range(waves)]
-    if taper and waves > 1:
-        a, b = out.pop()
-        while b - a > 1:
-            h = (b - a + 1) // 2
-            out.append((a, a + h))
-            a += h
-        out.append((a, b))
-    return out
+    return [(lo + w * n // waves, lo + (w + 1) * n // waves) for w in range(waves)]
 
 
 @dataclass
