@@ -138,6 +138,7 @@ class PeerOutput:
         from cuda.bindings import runtime as rt
 
         self._rt, self._group, self._dst = rt, group, dst
+        self.dst = dst
         self.rank = dist.get_rank(group)
         self.device = torch.device(device)
         self.nbytes = math.prod(shape) * torch.empty((), dtype=dtype).element_size()
@@ -199,7 +200,7 @@ class CopyGather:
 
     def __init__(self, peer: "PeerOutput", lo: int, out_local: torch.Tensor):
         self.peer, self.lo, self.out_local = peer, lo, out_local
-        self.send = peer.rank != peer._dst
+        self.send = peer.rank != peer.dst
         self.alt = torch.cuda.Stream(peer.device)
         self.copy = torch.cuda.Stream(peer.device)
 
